@@ -1,0 +1,258 @@
+"""Launch-configuration policy for the CUDA folds on B200.
+
+The reference picks Triton meta-parameters `(BLOCK, num_warps)` per shape bucket from a per-GPU
+measured table (neptune_codegen/autotune.py:222-250, table launch_table.py:23-49). This module keeps
+that policy and its vocabulary -- a `(block, num_warps)` pair, `(rows class, pow2 width bucket)`
+keys, a machine-keyed table holding only measured deviations from the default, a noise margin a
+candidate must clear -- but the pair now selects a CUDA launch:
+
+* ``num_warps == 1``: one warp folds one row (persistent CTAs of 8 warps, row chunks resident in
+  registers, no shared memory or barriers);
+* ``num_warps >= 2``: one CTA of ``32 * num_warps`` threads folds one row (cross-warp reduction
+  through shared memory);
+* ``block`` is the split plan's chunk width in columns (one CTA per chunk). The serial kernels size
+  their register tile from the row width themselves, so for the serial plan ``block`` only takes
+  part in the operator's identity.
+
+The default depends on the row's byte width (rows up to 16 KB fit a warp's registers), which is why
+it is a function here rather than a constant.
+"""
+from __future__ import annotations
+
+import dataclasses
+import hashlib
+import math
+
+from neptune_opt_b200._lib import VARIANT_CTA_ROW, VARIANT_WARP_ROW, launch_struct
+
+# Every configuration the search may choose from.
+CANDIDATES: tuple = (
+    (4096, 1), (16384, 1),
+    (4096, 4), (16384, 4),
+    (4096, 8), (16384, 8),
+    (16384, 16),
+)
+
+# The split plan's chunk width when nothing else is known: 16K columns per CTA (32 KB of bf16).
+SPLIT_BLOCK = 16384
+WARP_ROW_BYTES = 16384
+
+MIN_BUCKET = 256
+MAX_BUCKET = 1 << 22
+THIN_ROWS = 8
+NOISE = 0.05
+MACHINE = "b200"
+
+
+def machine_key(device_name: str | None = None) -> str:
+    """Normalised GPU name: 'NVIDIA B200' -> 'b200'."""
+    name = device_name
+    if name is None:
+        try:  # pragma: no cover - needs a GPU
+            import torch
+
+            if not torch.cuda.is_available():
+                return ""
+            name = torch.cuda.get_device_name(torch.cuda.current_device())
+        except Exception:  # noqa: BLE001
+            return ""
+    words = []
+    for word in str(name).lower().replace("+", " ").split():
+        if word in ("nvidia", "geforce", "tesla", "graphics", "corporation"):
+            continue
+        words.append("".join(ch if ch.isalnum() else "-" for ch in word).strip("-"))
+    return "-".join(w for w in words if w)
+
+
+def ncols_bucket(ncols) -> int:
+    if not isinstance(ncols, int):
+        raise ValueError("a measured width bucket requires a static integer width")
+    n = max(1, ncols)
+    return max(MIN_BUCKET, min(MAX_BUCKET, 1 << (n - 1).bit_length()))
+
+
+def rows_class(rows) -> str:
+    if not isinstance(rows, int):
+        return "many"
+    if rows <= 1:
+        return "single"
+    return "few" if rows <= THIN_ROWS else "many"
+
+
+def shape_key(rows, ncols) -> tuple:
+    return rows_class(rows), ncols_bucket(ncols)
+
+
+def _elem_bytes(dtype) -> int:
+    text = str(dtype)
+    return 4 if text.endswith("float32") or text == "float32" else 2
+
+
+def default_config(ncols=None, dtype=None) -> tuple:
+    """Warp per row while the row fits 16 KB, else a CTA of 8 warps per row."""
+    if not isinstance(ncols, int):
+        return (SPLIT_BLOCK, 1)
+    return (SPLIT_BLOCK, 1) if ncols * _elem_bytes(dtype) <= WARP_ROW_BYTES else (SPLIT_BLOCK, 8)
+
+
+DEFAULT = default_config()
+
+
+def _module_tables() -> dict:
+    try:
+        from neptune_opt_b200 import launch_table
+    except Exception:  # noqa: BLE001
+        return {}
+    out = {}
+    for machine, entry in getattr(launch_table, "TABLES", {}).items():
+        body = entry.get("table") or {}
+        out[machine] = {**{k: v for k, v in entry.items() if k != "table"}, "table": _valid(body)}
+    return out
+
+
+def _valid(body) -> dict:
+    return {tuple(k): tuple(v) for k, v in (body or {}).items() if tuple(v) in CANDIDATES}
+
+
+def tables() -> dict:
+    return _module_tables()
+
+
+def table(machine: str | None = None) -> dict:
+    """The measured deviations for one machine; never another machine's numbers."""
+    all_tables = tables()
+    if machine is None:
+        machine = machine_key()
+    return dict(all_tables.get(machine, {}).get("table", {}))
+
+
+def best_config(rows, ncols, dtype=None, device=None, device_name=None, verbose: bool = False) -> tuple:
+    """`(block, num_warps)` for a shape on this machine: measured entry, else the default."""
+    if not isinstance(rows, int) or not isinstance(ncols, int):
+        return default_config(ncols if isinstance(ncols, int) else None, dtype)
+    default = default_config(ncols, dtype)
+    if device is not None and str(device).split(":", 1)[0] != "cuda":
+        return default
+    if device_name is None and device is not None:
+        try:
+            import torch
+
+            device_name = torch.cuda.get_device_name(torch.device(device))
+        except Exception:  # noqa: BLE001
+            device_name = None
+    machine = machine_key(device_name) if device_name else ""
+    cfg = table(machine).get(shape_key(rows, ncols), default) if machine else default
+    if verbose:
+        print(f"launch config rows={rows} ncols={ncols} on {machine or '<unknown gpu>'}: {cfg}")
+    return cfg
+
+
+def launch_for(cfg) -> object | None:
+    """The C ABI launch struct for a `(block, num_warps)` pair (None: library default)."""
+    if cfg is None:
+        return None
+    _block, warps = cfg
+    if warps is None:
+        return None
+    if warps <= 1:
+        return launch_struct(VARIANT_WARP_ROW, 0, 0)
+    return launch_struct(VARIANT_CTA_ROW, 32 * int(warps), 0)
+
+
+# ---------------------------------------------------------------- the choice rule
+@dataclasses.dataclass
+class Result:
+    block: int
+    num_warps: int
+    ms: float
+
+    def __str__(self) -> str:
+        return f"block={self.block:6d} num_warps={self.num_warps:2d} {self.ms:8.4f} ms"
+
+
+def best_of(results: list) -> list:
+    ok = [r for r in results if math.isfinite(r.ms)]
+    if not ok:
+        raise RuntimeError(f"no candidate launch configuration could be measured ({len(results)} tried)")
+    return sorted(ok, key=lambda r: r.ms)
+
+
+def choose(results: list, default: tuple, noise: float = NOISE) -> tuple:
+    """Keep `default` unless the fastest candidate beats it by more than `noise`."""
+    ranked = best_of(results)
+    best = ranked[0]
+    fix = next((r for r in results if (r.block, r.num_warps) == tuple(default)), None)
+    if fix is None or best.ms <= 0:
+        return tuple(default), float("nan"), "the default was not measurable: keeping it"
+    gain = fix.ms / best.ms
+    if gain <= 1.0 + noise:
+        return tuple(default), gain, f"within noise ({gain:.2f}x): keeping the default"
+    return (best.block, best.num_warps), gain, f"{gain:.2f}x better than the default"
+
+
+def parameter_identity(params: dict | None) -> tuple:
+    """Exact identity of binary64 scalars (hex), as neptune_codegen/autotune.py:392-394."""
+    return tuple((key, float(value).hex()) for key, value in sorted((params or {}).items()))
+
+
+def parameter_tag(params: dict | None) -> str:
+    """Identifier-safe exact tag of the parameters (same scheme as autotune.py:397-418)."""
+    identity = parameter_identity(params)
+    tags = []
+    for key, exact in identity:
+        value = float.fromhex(exact)
+        short = f"{value:g}"
+        tag = short.replace(".", "p").replace("-", "m").replace("+", "a")
+        if not math.isfinite(value) or float(short).hex() != exact:
+            tag += "_h" + exact.replace("-", "m").replace("+", "a").replace(".", "p")
+        tags.append("_" + key + tag)
+    if len(identity) > 1 or any(not key.isalpha() for key, _ in identity):
+        tags.append("_h" + hashlib.sha256(repr(identity).encode()).hexdigest()[:16])
+    return "".join(tags)
+
+
+def op_key(lib: str, name: str, params: dict | None, keepdim: bool,
+           block: int | None = None, num_warps: int | None = None) -> str:
+    """Registered op name: parameters, output rank and launch configuration (autotune.py:421-432)."""
+    tag = "_keep" if keepdim else ""
+    tag += parameter_tag(params)
+    if block is not None or num_warps is not None:
+        tag += f"_b{block}w{num_warps}"
+    return f"{lib}::{name}{tag}"
+
+
+def search(name: str, rows: int, ncols: int, dtype=None, device: str = "cuda", reps: int = 50,
+           candidates=CANDIDATES, params: dict | None = None, warmup: int = 5, rounds: int = 3) -> list:
+    """Time every candidate through the C ABI with CUDA events; fastest first."""
+    import torch
+
+    from neptune_opt_b200 import template
+
+    if dtype is None:
+        dtype = torch.float32
+    x = torch.randn(rows, ncols, device=device, dtype=dtype).abs().contiguous()
+    out = torch.empty(rows, device=device, dtype=dtype)
+    results = []
+    for block, warps in candidates:
+        def launch(block=block, warps=warps):
+            template.launch_reduction(name, "serial", x, out, rows, ncols, block, warps, params)
+
+        try:
+            for _ in range(warmup):
+                launch()
+            torch.cuda.synchronize()
+        except Exception as exc:  # noqa: BLE001
+            results.append(Result(block, warps, float("inf")))
+            print(f"      block={block} num_warps={warps} cannot launch: {type(exc).__name__}: {exc}")
+            continue
+        times = []
+        for _ in range(rounds):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            for _ in range(reps):
+                launch()
+            end.record()
+            end.synchronize()
+            times.append(start.elapsed_time(end) / reps)
+        results.append(Result(block, warps, min(times)))
+    return best_of(results)

@@ -1,0 +1,454 @@
+// Row-last repaired folds on sm_100a: the serial plan (one warp or one CTA per row), the
+// softmax / log_softmax / L2-normalize readouts fused into the same single pass, and the explicit
+// split plan (chunk states + ordered merge).
+//
+// Reference kernels replaced: the serial template neptune_codegen/template.py:41-54 with its
+// helpers emitters.py:436-532, the two-pass template template.py:62-103 and the split pair
+// template.py:137-165 (launch template.py:368-390).
+#include "fold.cuh"
+#include "launch.h"
+
+namespace nb200 {
+
+// ------------------------------------------------------------------ serial fold
+template <int S, typename T, int NV, bool VEC, bool CTA>
+__global__ void __launch_bounds__(CTA ? 512 : 256)
+fold_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t rows, int64_t ncols,
+            int64_t srow, int64_t scol, Params p) {
+    __shared__ float red[64];
+    Group<CTA> grp{red, 0};
+    const int G = CTA ? (int)blockDim.x : 32;
+    const int t = CTA ? (int)threadIdx.x : (int)(threadIdx.x & 31);
+    const int64_t gid = CTA ? (int64_t)blockIdx.x
+                            : (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t ng = CTA ? (int64_t)gridDim.x : (int64_t)gridDim.x * (blockDim.x >> 5);
+    using CH = Chunk<T, NV, VEC>;
+    const int64_t span = (int64_t)G * CH::E;
+    for (int64_t r = gid; r < rows; r += ng) {
+        const T* row = x + r * srow;
+        float res;
+        if constexpr (Sk<S>::kind == K_TWOPASS) {
+            // pass 1: the producer (mean as sum of c / N); pass 2: the centred term with the
+            // producer held constant. A resident row is not read twice.
+            const bool resident = span >= ncols;
+            CH ch;
+            float mean = 0.f;
+            for (int64_t c0 = 0; c0 < ncols; c0 += span) {
+                ch.load(row, scol, c0, ncols, t, G, false);
+                float s = 0.f;
+#pragma unroll
+                for (int i = 0; i < CH::E; ++i)
+                    if (CH::valid(c0, ncols, t, G, i)) s += ch.get(i) * p.invN;
+                mean = mean + grp.reduce(s, RED_SUM);
+            }
+            float acc = 0.f;
+            for (int64_t c0 = 0; c0 < ncols; c0 += span) {
+                if (!resident) ch.load(row, scol, c0, ncols, t, G, true);
+                float s = 0.f;
+#pragma unroll
+                for (int i = 0; i < CH::E; ++i) {
+                    if (CH::valid(c0, ncols, t, G, i)) {
+                        const float d = ch.get(i) - mean;
+                        s += p.invN * (d * d);
+                    }
+                }
+                acc = acc + grp.reduce(s, RED_SUM);
+            }
+            res = Sk<S>::fin(acc);
+        } else {
+            St run = empty_state();
+            for (int64_t c0 = 0; c0 < ncols; c0 += span) {
+                CH ch;
+                ch.load(row, scol, c0, ncols, t, G, true);
+                run = merge<S>(run, chunk_state<S>(ch, c0, ncols, t, G, grp, p), p);
+            }
+            res = finalize<S>(run, p);
+        }
+        if (t == 0) out[r] = Elem<T>::from_f(res);
+    }
+}
+
+// ------------------------------------------------------------------ softmax-family readout
+// mode 0: softmax = exp(x - m) / s; mode 1: log_softmax = (x - m) - log(s). A row with NaN, +inf
+// or no finite element reads out as NaN everywhere, as the reference's lowering does
+// (neptune_recognize/lowering.py:91-99). Rows that fit the chunk are read from HBM once.
+template <typename T, int NV, bool VEC, bool CTA>
+__global__ void __launch_bounds__(CTA ? 512 : 256)
+softmax_kernel(const T* __restrict__ x, T* __restrict__ y, T* __restrict__ lse, int64_t rows,
+               int64_t ncols, int64_t srow, int64_t scol, int mode, int out_vec) {
+    __shared__ float red[64];
+    Group<CTA> grp{red, 0};
+    const int G = CTA ? (int)blockDim.x : 32;
+    const int t = CTA ? (int)threadIdx.x : (int)(threadIdx.x & 31);
+    const int64_t gid = CTA ? (int64_t)blockIdx.x
+                            : (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t ng = CTA ? (int64_t)gridDim.x : (int64_t)gridDim.x * (blockDim.x >> 5);
+    using CH = Chunk<T, NV, VEC>;
+    const int64_t span = (int64_t)G * CH::E;
+    const bool resident = span >= ncols;
+    const Params p{0.f, 0.f, 1.f, 1.f, 0.f, 0.f, 0.f};
+    for (int64_t r = gid; r < rows; r += ng) {
+        const T* row = x + r * srow;
+        CH ch;
+        St run = empty_state();
+        for (int64_t c0 = 0; c0 < ncols; c0 += span) {
+            ch.load(row, scol, c0, ncols, t, G, resident);
+            run = merge<NB200_LOGSUMEXP>(run, chunk_state<NB200_LOGSUMEXP>(ch, c0, ncols, t, G, grp, p), p);
+        }
+        const bool bad = run.status != 0 || !run.seen;
+        const float m = run.m, inv = 1.0f / run.acc, lg = logf(run.acc);
+        T* yrow = y + r * ncols;
+        for (int64_t c0 = 0; c0 < ncols; c0 += span) {
+            if (!resident) ch.load(row, scol, c0, ncols, t, G, false);
+#pragma unroll
+            for (int k = 0; k < NV; ++k) {
+                float f[CH::V];
+#pragma unroll
+                for (int j = 0; j < CH::V; ++j) {
+                    const float v = ch.get(k * CH::V + j);
+                    f[j] = bad ? NB200_NAN : (mode == 0 ? expf(v - m) * inv : (v - m) - lg);
+                }
+                store_vec<T, NV, VEC>(yrow, f, k, c0, ncols, t, G, out_vec != 0);
+            }
+        }
+        if (lse != nullptr && t == 0) lse[r] = Elem<T>::from_f(finalize<NB200_LOGSUMEXP>(run, p));
+    }
+}
+
+// ------------------------------------------------------------------ L2 normalize readout
+template <typename T, int NV, bool VEC, bool CTA>
+__global__ void __launch_bounds__(CTA ? 512 : 256)
+l2norm_kernel(const T* __restrict__ x, T* __restrict__ y, T* __restrict__ norm, int64_t rows,
+              int64_t ncols, int64_t srow, int64_t scol, int out_vec) {
+    __shared__ float red[64];
+    Group<CTA> grp{red, 0};
+    const int G = CTA ? (int)blockDim.x : 32;
+    const int t = CTA ? (int)threadIdx.x : (int)(threadIdx.x & 31);
+    const int64_t gid = CTA ? (int64_t)blockIdx.x
+                            : (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t ng = CTA ? (int64_t)gridDim.x : (int64_t)gridDim.x * (blockDim.x >> 5);
+    using CH = Chunk<T, NV, VEC>;
+    const int64_t span = (int64_t)G * CH::E;
+    const bool resident = span >= ncols;
+    const Params p{0.f, 0.f, 1.f, 1.f, 0.f, 0.f, 0.f};
+    for (int64_t r = gid; r < rows; r += ng) {
+        const T* row = x + r * srow;
+        CH ch;
+        St run = empty_state();
+        for (int64_t c0 = 0; c0 < ncols; c0 += span) {
+            ch.load(row, scol, c0, ncols, t, G, resident);
+            run = merge<NB200_STABLE_L2>(run, chunk_state<NB200_STABLE_L2>(ch, c0, ncols, t, G, grp, p), p);
+        }
+        const float nrm = finalize<NB200_STABLE_L2>(run, p);
+        T* yrow = y + r * ncols;
+        for (int64_t c0 = 0; c0 < ncols; c0 += span) {
+            if (!resident) ch.load(row, scol, c0, ncols, t, G, false);
+#pragma unroll
+            for (int k = 0; k < NV; ++k) {
+                float f[CH::V];
+#pragma unroll
+                for (int j = 0; j < CH::V; ++j) f[j] = __fdiv_rn(ch.get(k * CH::V + j), nrm);
+                store_vec<T, NV, VEC>(yrow, f, k, c0, ncols, t, G, out_vec != 0);
+            }
+        }
+        if (norm != nullptr && t == 0) norm[r] = Elem<T>::from_f(nrm);
+    }
+}
+
+// ------------------------------------------------------------------ split plan
+// One CTA per (row, part): the state of columns [cb + part * cc, min(cb + (part+1) * cc, cb + ns)).
+template <int S, typename T, bool VEC>
+__global__ void __launch_bounds__(256)
+partial_kernel(const T* __restrict__ x, nb200_state* __restrict__ states, int64_t rows, int64_t cb,
+               int64_t ns, int64_t srow, int64_t scol, int64_t cc, int64_t nparts, Params p) {
+    __shared__ float red[64];
+    Group<true> grp{red, 0};
+    const int G = (int)blockDim.x, t = (int)threadIdx.x;
+    using CH = Chunk<T, 4, VEC>;
+    const int64_t span = (int64_t)G * CH::E;
+    const int64_t work = rows * nparts;
+    for (int64_t w = blockIdx.x; w < work; w += gridDim.x) {
+        const int64_t r = w / nparts, part = w - r * nparts;
+        const T* row = x + r * srow;
+        const int64_t lo = cb + part * cc;
+        const int64_t hi = min(lo + cc, cb + ns);
+        St run = empty_state();
+        for (int64_t c0 = lo; c0 < hi; c0 += span) {
+            CH ch;
+            ch.load(row, scol, c0, hi, t, G, true);
+            run = merge<S>(run, chunk_state<S>(ch, c0, hi, t, G, grp, p), p);
+        }
+        if (t == 0)
+            reinterpret_cast<float4*>(states)[w] =
+                make_float4(run.m, run.acc, __int_as_float(run.seen), __int_as_float(run.status));
+    }
+}
+
+__device__ __forceinline__ St shfl_state(const St& s, int o) {
+    St r;
+    r.m = __shfl_xor_sync(0xffffffffu, s.m, o);
+    r.acc = __shfl_xor_sync(0xffffffffu, s.acc, o);
+    r.seen = __shfl_xor_sync(0xffffffffu, s.seen, o);
+    r.status = __shfl_xor_sync(0xffffffffu, s.status, o);
+    return r;
+}
+
+// One warp per row. Lane l folds the contiguous run of parts [l*k, (l+1)*k) left to right; the
+// 32 runs then combine in a fixed balanced tree, always with the lower-indexed run on the left.
+// The order depends only on nparts, so the result is deterministic.
+template <int S, typename T>
+__global__ void __launch_bounds__(256)
+merge_kernel(const nb200_state* __restrict__ states, T* __restrict__ out, int64_t rows,
+             int64_t nparts, int64_t rstride, int64_t pstride, Params p) {
+    const int lane = threadIdx.x & 31;
+    const int64_t gid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t ng = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int64_t k = (nparts + 31) / 32;
+    for (int64_t r = gid; r < rows; r += ng) {
+        St s = empty_state();
+        const int64_t lo = (int64_t)lane * k;
+        const int64_t hi = min(lo + k, nparts);
+        for (int64_t j = lo; j < hi; ++j) {
+            const nb200_state b = states[r * rstride + j * pstride];
+            s = merge<S>(s, St{b.m, b.acc, b.seen, b.status}, p);
+        }
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const St other = shfl_state(s, o);
+            s = (lane & o) ? merge<S>(other, s, p) : merge<S>(s, other, p);
+        }
+        if (lane == 0) out[r] = Elem<T>::from_f(finalize<S>(s, p));
+    }
+}
+
+// ================================================================== host side
+Params make_params(const nb200_params& q, int64_t ncols) {
+    Params p;
+    p.tiny = (float)q.tiny;
+    p.alpha = (float)q.alpha;
+    p.invT = q.T != 0.0 ? (float)(1.0 / q.T) : 0.f;
+    p.beta = (float)q.beta;
+    p.N = (float)q.N;
+    p.eps = (float)q.eps;
+    p.invN = ncols > 0 ? (float)(1.0 / (double)ncols) : 0.f;
+    return p;
+}
+
+namespace {
+
+constexpr int kWarpThreads = 256;
+
+template <typename T>
+bool rows_vectorizable(const T* x, int64_t rows, int64_t ncols, int64_t srow, int64_t scol) {
+    constexpr int V = Elem<T>::V;
+    return scol == 1 && aligned16(x) && (rows <= 1 || (srow * (int64_t)sizeof(T)) % 16 == 0) &&
+           ncols % V == 0;
+}
+
+template <int S, typename T>
+int fold_t(const T* x, T* out, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
+           const Params& p, const nb200_launch* L, cudaStream_t st) {
+    const bool vec = rows_vectorizable(x, rows, ncols, srow, scol);
+    const int64_t bytes = ncols * (int64_t)sizeof(T);
+    int variant = (L && L->variant) ? L->variant : (bytes <= 16384 ? NB200_VARIANT_WARP_ROW : NB200_VARIANT_CTA_ROW);
+    const int cps = L ? L->ctas_per_sm : 0;
+    if (variant == NB200_VARIANT_WARP_ROW) {
+        auto k = vec ? fold_kernel<S, T, 4, true, false> : fold_kernel<S, T, kScalarNV<T>, false, false>;
+        const int g = persistent_grid(k, kWarpThreads, 0, (rows + 7) / 8, cps);
+        k<<<g, kWarpThreads, 0, st>>>(x, out, rows, ncols, srow, scol, p);
+    } else {
+        int threads = (L && L->threads) ? L->threads : (bytes >= 65536 ? 512 : 256);
+        auto k = vec ? fold_kernel<S, T, 4, true, true> : fold_kernel<S, T, kScalarNV<T>, false, true>;
+        const int g = persistent_grid(k, threads, 0, rows, cps);
+        k<<<g, threads, 0, st>>>(x, out, rows, ncols, srow, scol, p);
+    }
+    count_launch();
+    return finish_launch("nb200_fold");
+}
+
+template <typename T>
+int fold_dispatch(int sk, const T* x, T* out, int64_t rows, int64_t ncols, int64_t srow,
+                  int64_t scol, const Params& p, const nb200_launch* L, cudaStream_t st) {
+    switch (sk) {
+        case NB200_LOGSUMEXP: return fold_t<NB200_LOGSUMEXP, T>(x, out, rows, ncols, srow, scol, p, L, st);
+        case NB200_LSE_BIASED: return fold_t<NB200_LSE_BIASED, T>(x, out, rows, ncols, srow, scol, p, L, st);
+        case NB200_LSE_SCALED: return fold_t<NB200_LSE_SCALED, T>(x, out, rows, ncols, srow, scol, p, L, st);
+        case NB200_SOFTCAP_LSE: return fold_t<NB200_SOFTCAP_LSE, T>(x, out, rows, ncols, srow, scol, p, L, st);
+        case NB200_STABLE_L2: return fold_t<NB200_STABLE_L2, T>(x, out, rows, ncols, srow, scol, p, L, st);
+        case NB200_LINEAR_ATTN: return fold_t<NB200_LINEAR_ATTN, T>(x, out, rows, ncols, srow, scol, p, L, st);
+        case NB200_DECAY_RENORM: return fold_t<NB200_DECAY_RENORM, T>(x, out, rows, ncols, srow, scol, p, L, st);
+        case NB200_SUMSQ_DIV: return fold_t<NB200_SUMSQ_DIV, T>(x, out, rows, ncols, srow, scol, p, L, st);
+        case NB200_RMSNORM_MAX: return fold_t<NB200_RMSNORM_MAX, T>(x, out, rows, ncols, srow, scol, p, L, st);
+        case NB200_VARIANCE: return fold_t<NB200_VARIANCE, T>(x, out, rows, ncols, srow, scol, p, L, st);
+        case NB200_STD: return fold_t<NB200_STD, T>(x, out, rows, ncols, srow, scol, p, L, st);
+    }
+    set_error("unknown skeleton %d", sk);
+    return NB200_ERR_ARG;
+}
+
+// Chooses the register tile so that a row fits one chunk whenever it can: a warp per row up to
+// 16 vectors per lane, then a CTA per row, then chunked (two reads of the row).
+template <typename T, template <typename, int, bool, bool> class KS>
+struct ReadoutPlan {
+    template <typename F>
+    static int run(const T* x, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
+                   const nb200_launch* L, cudaStream_t st, F&& launch) {
+        constexpr int V = Elem<T>::V;
+        const bool vec = rows_vectorizable(x, rows, ncols, srow, scol);
+        const int cps = L ? L->ctas_per_sm : 0;
+        const int64_t vecs = (ncols + V - 1) / V;  // 16-byte vectors per row
+        int variant = (L && L->variant) ? L->variant : (vecs <= 32 * 16 ? NB200_VARIANT_WARP_ROW : NB200_VARIANT_CTA_ROW);
+        if (!vec) {
+            if (variant == NB200_VARIANT_WARP_ROW) {
+                auto k = KS<T, kScalarNV<T>, false, false>::get();
+                return launch(k, persistent_grid(k, kWarpThreads, 0, (rows + 7) / 8, cps), kWarpThreads);
+            }
+            const int threads = (L && L->threads) ? L->threads : 256;
+            auto k = KS<T, kScalarNV<T>, false, true>::get();
+            return launch(k, persistent_grid(k, threads, 0, rows, cps), threads);
+        }
+        if (variant == NB200_VARIANT_WARP_ROW) {
+            const int64_t per_lane = (vecs + 31) / 32;
+            auto pick = [&]() {
+                if (per_lane <= 1) return KS<T, 1, true, false>::get();
+                if (per_lane <= 2) return KS<T, 2, true, false>::get();
+                if (per_lane <= 4) return KS<T, 4, true, false>::get();
+                if (per_lane <= 8) return KS<T, 8, true, false>::get();
+                return KS<T, 16, true, false>::get();
+            };
+            auto k = pick();
+            return launch(k, persistent_grid(k, kWarpThreads, 0, (rows + 7) / 8, cps), kWarpThreads);
+        }
+        const int threads = (L && L->threads) ? L->threads : 256;
+        const int64_t per_thread = (vecs + threads - 1) / threads;
+        auto pick = [&]() {
+            if (per_thread <= 4) return KS<T, 4, true, true>::get();
+            if (per_thread <= 8) return KS<T, 8, true, true>::get();
+            return KS<T, 16, true, true>::get();
+        };
+        auto k = pick();
+        return launch(k, persistent_grid(k, threads, 0, rows, cps), threads);
+    }
+};
+
+template <typename T, int NV, bool VEC, bool CTA>
+struct SoftmaxK {
+    static auto get() { return softmax_kernel<T, NV, VEC, CTA>; }
+};
+template <typename T, int NV, bool VEC, bool CTA>
+struct L2K {
+    static auto get() { return l2norm_kernel<T, NV, VEC, CTA>; }
+};
+
+template <typename T>
+int softmax_t(int mode, const T* x, T* y, T* lse, int64_t rows, int64_t ncols, int64_t srow,
+              int64_t scol, const nb200_launch* L, cudaStream_t st) {
+    const int out_vec = aligned16(y) && (ncols * (int64_t)sizeof(T)) % 16 == 0;
+    return ReadoutPlan<T, SoftmaxK>::run(x, rows, ncols, srow, scol, L, st, [&](auto k, int g, int th) {
+        k<<<g, th, 0, st>>>(x, y, lse, rows, ncols, srow, scol, mode, out_vec);
+        count_launch();
+        return finish_launch("nb200_softmax");
+    });
+}
+
+template <typename T>
+int l2_t(const T* x, T* y, T* norm, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
+         const nb200_launch* L, cudaStream_t st) {
+    const int out_vec = aligned16(y) && (ncols * (int64_t)sizeof(T)) % 16 == 0;
+    return ReadoutPlan<T, L2K>::run(x, rows, ncols, srow, scol, L, st, [&](auto k, int g, int th) {
+        k<<<g, th, 0, st>>>(x, y, norm, rows, ncols, srow, scol, out_vec);
+        count_launch();
+        return finish_launch("nb200_l2_normalize");
+    });
+}
+
+template <int S, typename T>
+int partial_t(const T* x, nb200_state* states, int64_t rows, int64_t cb, int64_t ns, int64_t srow,
+              int64_t scol, int64_t cc, int64_t nparts, const Params& p, cudaStream_t st) {
+    constexpr int V = Elem<T>::V;
+    const bool vec = rows_vectorizable(x, rows, cb + ns, srow, scol) && cb % V == 0 && cc % V == 0;
+    auto k = vec ? partial_kernel<S, T, true> : partial_kernel<S, T, false>;
+    const int g = persistent_grid(k, 256, 0, rows * nparts, 0);
+    k<<<g, 256, 0, st>>>(x, states, rows, cb, ns, srow, scol, cc, nparts, p);
+    count_launch();
+    return finish_launch("nb200_fold_partial");
+}
+
+template <int S, typename T>
+int merge_t(const nb200_state* states, T* out, int64_t rows, int64_t nparts, int64_t rs, int64_t ps,
+            const Params& p, cudaStream_t st) {
+    auto k = merge_kernel<S, T>;
+    const int g = persistent_grid(k, 256, 0, (rows + 7) / 8, 0);
+    k<<<g, 256, 0, st>>>(states, out, rows, nparts, rs, ps, p);
+    count_launch();
+    return finish_launch("nb200_fold_merge");
+}
+
+#define NB200_SPLIT_SKELETONS(X)                                                              \
+    X(NB200_LOGSUMEXP) X(NB200_LSE_BIASED) X(NB200_LSE_SCALED) X(NB200_SOFTCAP_LSE)           \
+    X(NB200_STABLE_L2) X(NB200_LINEAR_ATTN) X(NB200_DECAY_RENORM) X(NB200_SUMSQ_DIV)          \
+    X(NB200_RMSNORM_MAX)
+
+template <typename T>
+int partial_dispatch(int sk, const T* x, nb200_state* states, int64_t rows, int64_t cb, int64_t ns,
+                     int64_t srow, int64_t scol, int64_t cc, int64_t nparts, const Params& p,
+                     cudaStream_t st) {
+    switch (sk) {
+#define X(S) case S: return partial_t<S, T>(x, states, rows, cb, ns, srow, scol, cc, nparts, p, st);
+        NB200_SPLIT_SKELETONS(X)
+#undef X
+    }
+    set_error("skeleton %d has no split plan (two-pass skeletons need extended carried state)", sk);
+    return NB200_ERR_UNSUPPORTED;
+}
+
+template <typename T>
+int merge_dispatch(int sk, const nb200_state* states, T* out, int64_t rows, int64_t nparts,
+                   int64_t rs, int64_t ps, const Params& p, cudaStream_t st) {
+    switch (sk) {
+#define X(S) case S: return merge_t<S, T>(states, out, rows, nparts, rs, ps, p, st);
+        NB200_SPLIT_SKELETONS(X)
+#undef X
+    }
+    set_error("skeleton %d has no split plan (two-pass skeletons need extended carried state)", sk);
+    return NB200_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+#define NB200_DTYPE_CASES(dtype, CALL)                                                  \
+    switch (dtype) {                                                                  \
+        case NB200_F32: { using T = float; return CALL; }                              \
+        case NB200_BF16: { using T = __nv_bfloat16; return CALL; }                     \
+        case NB200_F16: { using T = __half; return CALL; }                             \
+    }                                                                                 \
+    set_error("unknown dtype %d", dtype);                                             \
+    return NB200_ERR_ARG;
+
+int launch_fold(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t ncols,
+                int64_t srow, int64_t scol, void* out, const nb200_launch* L, cudaStream_t st) {
+    NB200_DTYPE_CASES(dtype, fold_dispatch<T>(sk, (const T*)x, (T*)out, rows, ncols, srow, scol, p, L, st))
+}
+
+int launch_softmax(int mode, const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow,
+                   int64_t scol, void* y, void* lse, const nb200_launch* L, cudaStream_t st) {
+    NB200_DTYPE_CASES(dtype, softmax_t<T>(mode, (const T*)x, (T*)y, (T*)lse, rows, ncols, srow, scol, L, st))
+}
+
+int launch_l2(const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
+              void* y, void* norm, const nb200_launch* L, cudaStream_t st) {
+    NB200_DTYPE_CASES(dtype, l2_t<T>((const T*)x, (T*)y, (T*)norm, rows, ncols, srow, scol, L, st))
+}
+
+int launch_partial(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t cb,
+                   int64_t ns, int64_t srow, int64_t scol, int64_t cc, int64_t nparts,
+                   nb200_state* states, cudaStream_t st) {
+    NB200_DTYPE_CASES(dtype, partial_dispatch<T>(sk, (const T*)x, states, rows, cb, ns, srow, scol, cc, nparts, p, st))
+}
+
+int launch_merge(int sk, const Params& p, const nb200_state* states, int64_t rows, int64_t nparts,
+                 int64_t rs, int64_t ps, void* out, int dtype, cudaStream_t st) {
+    NB200_DTYPE_CASES(dtype, merge_dispatch<T>(sk, states, (T*)out, rows, nparts, rs, ps, p, st))
+}
+
+}  // namespace nb200

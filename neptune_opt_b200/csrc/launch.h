@@ -1,0 +1,41 @@
+// Internal host-side launchers shared by the kernel files and the C ABI (capi.cu). All return an
+// nb200_status and record a message on failure.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/neptune_b200.h"
+
+namespace nb200 {
+
+struct Params;
+Params make_params(const nb200_params& q, int64_t ncols);
+
+int launch_fold(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t ncols,
+                int64_t srow, int64_t scol, void* out, const nb200_launch* L, cudaStream_t st);
+int launch_softmax(int mode, const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow,
+                   int64_t scol, void* y, void* lse, const nb200_launch* L, cudaStream_t st);
+int launch_l2(const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
+              void* y, void* norm, const nb200_launch* L, cudaStream_t st);
+int launch_partial(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t cb,
+                   int64_t ns, int64_t srow, int64_t scol, int64_t cc, int64_t nparts,
+                   nb200_state* states, cudaStream_t st);
+int launch_merge(int sk, const Params& p, const nb200_state* states, int64_t rows, int64_t nparts,
+                 int64_t rs, int64_t ps, void* out, int dtype, cudaStream_t st);
+
+int launch_rms(const void* x, const void* gamma, int dtype, int64_t rows, int64_t ncols,
+               int64_t srow, int64_t scol, int64_t sg, float eps, void* out,
+               const nb200_launch* L, cudaStream_t st);
+
+int launch_spans(const void* seg, int idt, int64_t nseg, int64_t sstride, int is_offsets,
+                 int unsafe, int64_t nrows, int64_t* spans, uint32_t* status, cudaStream_t st);
+int launch_segment_pool(const void* data, int dtype, int64_t nrows, int64_t channels,
+                        int64_t srow, int64_t sch, const int64_t* spans, int64_t nseg, int reduce,
+                        int has_initial, uint32_t initial_bits, void* out, cudaStream_t st);
+
+int launch_attention(const void* q, const void* k, const void* v, void* o, float* lse,
+                     int64_t B, int64_t H, int64_t S, int64_t D, int causal, float scale,
+                     cudaStream_t st);
+
+}  // namespace nb200
