@@ -1,0 +1,169 @@
+"""Multi-GPU partitioning of the fused reductions: one process per GPU, torch.distributed plumbing.
+
+The reference has no multi-GPU path (its roadmap declares it out of scope). Here every region
+partitions into independent units, so ranks need no data-path collective:
+
+* row-last folds, softmax, L2-normalize, RMSNorm: contiguous blocks of rows (`shard_rows`);
+* ordered segment pooling: contiguous blocks of whole segments, cut where the token counts balance
+  (`shard_segments`); each segment stays on one rank, so the storage-dtype rounding order -- and
+  with it the bit-exact result -- is unchanged;
+* attention: blocks of (batch, head) pairs (`shard_heads`).
+
+The one exchange is the split plan for ultra-wide rows when the reduction axis itself is sharded
+across GPUs (`sharded_split_fold`): each rank folds its column shard into per-row chunk states
+(16 bytes each), one all-gather moves them (a few KB per rank), and every rank merges them in
+ascending (rank, chunk) order -- the same certified order as the single-GPU split plan.
+"""
+from __future__ import annotations
+
+import ctypes
+import dataclasses
+
+
+def shard_rows(rows: int, world: int, rank: int) -> tuple:
+    """[begin, end) of rank's contiguous row block; blocks differ in size by at most one row."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    base, extra = divmod(rows, world)
+    begin = rank * base + min(rank, extra)
+    return begin, begin + base + (1 if rank < extra else 0)
+
+
+def shard_heads(batch: int, heads: int, world: int, rank: int) -> tuple:
+    """[begin, end) over the flattened batch*heads pairs."""
+    return shard_rows(batch * heads, world, rank)
+
+
+@dataclasses.dataclass(frozen=True)
+class SegmentShard:
+    seg_begin: int       # first segment of this rank
+    seg_end: int         # one past the last segment
+    row_begin: int       # first data row those segments read
+    row_end: int         # one past the last data row
+
+
+def shard_segments(offsets, world: int, rank: int) -> SegmentShard:
+    """Contiguous segments whose token ranges split the data rows evenly.
+
+    `offsets` is the CSR boundary array (length nsegments + 1, nondecreasing, host or device). The
+    cut before rank r is the first segment boundary at or after r * T / world, so every rank gets
+    whole segments and about T / world rows.
+    """
+    import torch
+
+    off = torch.as_tensor(offsets).to("cpu", torch.int64)
+    nseg = off.numel() - 1
+    if nseg < 0:
+        raise ValueError("offsets needs at least one boundary")
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    first, last = int(off[0]), int(off[-1])
+    total = last - first
+
+    def cut(r):
+        if r <= 0:
+            return 0
+        if r >= world:
+            return nseg
+        target = first + (total * r + world - 1) // world
+        return int(torch.searchsorted(off[:-1].contiguous(), torch.tensor(target), right=False))
+
+    s0, s1 = cut(rank), cut(rank + 1)
+    s1 = max(s0, s1)
+    return SegmentShard(s0, s1, int(off[s0]), int(off[s1]))
+
+
+def local_offsets(offsets, shard: SegmentShard):
+    """The rank's offsets rebased to its own data rows (first entry 0)."""
+    import torch
+
+    off = torch.as_tensor(offsets)
+    return off[shard.seg_begin:shard.seg_end + 1] - off[shard.seg_begin]
+
+
+# ---------------------------------------------------------------- the sharded split plan
+def _cuda_partial(name, params, x_shard, col_begin, ncols_total, chunk):
+    """Chunk states [rows, nparts] (as int32 [rows, nparts, 4]) of a column shard, via the C ABI."""
+    import torch
+
+    from neptune_opt_b200 import _lib
+    from neptune_opt_b200.skeletons import SKELETONS, checked_params
+    from neptune_opt_b200.template import _on_device, current_stream, dtype_code
+
+    rows, width = x_shard.shape
+    nparts = -(-width // chunk)
+    states = torch.empty(rows, nparts, 4, dtype=torch.int32, device=x_shard.device)
+    p = _lib.params_struct(checked_params(name, params))
+    lib = _lib.load()
+    with _on_device(x_shard.device):
+        rc = lib.nb200_fold_partial(SKELETONS[name].id, ctypes.byref(p), ctypes.c_void_p(x_shard.data_ptr()),
+                                    dtype_code(x_shard.dtype), rows, ncols_total, 0, width, x_shard.stride(0),
+                                    x_shard.stride(1), chunk, ctypes.c_void_p(states.data_ptr()),
+                                    ctypes.c_void_p(current_stream(x_shard.device)))
+    _lib.check(rc, f"neptune {name} partial")
+    return states
+
+
+def _cuda_merge(name, params, states, out):
+    """Merge [rows, nparts, 4] states in ascending part order into out[rows] via the C ABI."""
+    from neptune_opt_b200 import _lib
+    from neptune_opt_b200.skeletons import SKELETONS, checked_params
+    from neptune_opt_b200.template import _on_device, current_stream, dtype_code
+
+    rows, nparts = states.shape[0], states.shape[1]
+    p = _lib.params_struct(checked_params(name, params))
+    lib = _lib.load()
+    with _on_device(states.device):
+        rc = lib.nb200_fold_merge(SKELETONS[name].id, ctypes.byref(p), ctypes.c_void_p(states.data_ptr()), rows,
+                                  nparts, states.stride(0) // 4, states.stride(1) // 4,
+                                  ctypes.c_void_p(out.data_ptr()), dtype_code(out.dtype),
+                                  ctypes.c_void_p(current_stream(states.device)))
+    _lib.check(rc, f"neptune {name} merge")
+    return out
+
+
+def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: int = 16384, group=None,
+                       partial_fn=None, merge_fn=None):
+    """Fold rows whose columns are sharded across the ranks of `group`, rank order = column order.
+
+    Each rank passes its own [rows, width_r] block (the ranks' blocks concatenated along columns in
+    rank order form the full rows). Returns out[rows] in x's dtype on every rank. Communication: one
+    all-gather of the per-row chunk states (16 bytes per state). Shards of unequal width are padded
+    with empty states, which the merge skips.
+
+    `partial_fn(name, params, x_shard, col_begin, ncols_total, chunk) -> int32 [rows, nparts, 4]` and
+    `merge_fn(name, params, states, out)` default to the CUDA kernels; tests on CPU ranks substitute
+    their own to exercise the sharding and exchange logic.
+    """
+    import torch
+    import torch.distributed as td
+
+    from neptune_opt_b200.skeletons import SKELETONS
+
+    if SKELETONS[name].two_pass:
+        raise NotImplementedError("two_pass needs extended carried state; split refused")
+    partial_fn = partial_fn or _cuda_partial
+    merge_fn = merge_fn or _cuda_merge
+    world = td.get_world_size(group)
+    rank = td.get_rank(group)
+    rows, width = x_shard.shape
+    widths = torch.tensor([width], dtype=torch.int64, device=x_shard.device)
+    all_widths = [torch.zeros_like(widths) for _ in range(world)]
+    td.all_gather(all_widths, widths, group=group)
+    all_widths = [int(w.item()) for w in all_widths]
+    if sum(all_widths) != ncols_total:
+        raise ValueError(f"column shards sum to {sum(all_widths)}, expected {ncols_total}")
+    col_begin = sum(all_widths[:rank])
+    max_parts = max(-(-w // chunk) for w in all_widths)
+    local = partial_fn(name, params, x_shard, col_begin, ncols_total, chunk)
+    if local.shape[1] < max_parts:  # pad with empty (seen = 0) states
+        pad = torch.zeros(rows, max_parts - local.shape[1], 4, dtype=local.dtype, device=local.device)
+        pad[..., 0] = torch.tensor(float("-inf")).view(torch.int32) if local.dtype == torch.int32 else 0
+        local = torch.cat([local, pad], dim=1)
+    gathered = torch.empty((world * rows,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    td.all_gather_into_tensor(gathered, local.contiguous(), group=group)
+    gathered = gathered.view((world,) + tuple(local.shape))
+    # [world, rows, parts, 4] -> [rows, world * parts, 4]: ascending rank, then ascending chunk
+    states = gathered.permute(1, 0, 2, 3).reshape(rows, world * max_parts, 4).contiguous()
+    out = torch.empty(rows, dtype=x_shard.dtype, device=x_shard.device)
+    return merge_fn(name, params, states, out)
