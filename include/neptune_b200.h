@@ -73,7 +73,8 @@ typedef struct {
 typedef enum {
     NB200_VARIANT_AUTO = 0,
     NB200_VARIANT_WARP_ROW = 1, /* one warp folds one row, register-resident chunks     */
-    NB200_VARIANT_CTA_ROW = 2   /* one CTA folds one row                                 */
+    NB200_VARIANT_CTA_ROW = 2,  /* one CTA folds one row                                 */
+    NB200_VARIANT_STREAM = 3    /* bulk-copy staged rows (contiguous, 16-byte aligned)   */
 } nb200_variant;
 
 typedef struct {
@@ -97,6 +98,10 @@ const char* nb200_last_error(void);
 const char* nb200_version(void);
 /* Number of nb200 kernel launches issued by this process (for launch accounting). */
 uint64_t nb200_launch_count(void);
+/* Reads and clears the fault bits of the streaming kernels (bit 0: a bounded wait on a bulk copy
+ * ran out and the kernel stopped early). Synchronous. No counterpart in the reference, whose
+ * Triton kernels have no device-side waits. */
+int nb200_stream_fault(uint32_t* bits);
 
 /* ------------------------------------------------------------------ a1: serial fold
  * Row-last repaired fold of one skeleton over a strided 2-D view x[rows, ncols]
@@ -162,26 +167,29 @@ int nb200_rms_norm(const void* x, const void* gamma, int dtype, int64_t rows, in
                    double eps, void* out, const nb200_launch* launch, void* stream);
 
 /* ------------------------------------------------------------------ a4/a5: segments
- * Span construction (neptune_codegen/torch_op.py:370-387): from lengths (is_offsets = 0)
- * or offsets (is_offsets = 1) with element stride seg_stride, write int64
- * spans[nsegments + 1]. Validation never traps: violations set bits in *status
- * (device word, caller-zeroed): 1 negative/oversized length, 2 lengths do not cover
- * nrows (checked unless unsafe), 4 boundary out of [0, nrows], 8 non-monotonic.
- * nsegments is the number of segments (len(lengths) or len(offsets) - 1). */
-int nb200_segment_spans(const void* segments, int index_dtype, int64_t nsegments,
-                        int64_t seg_stride, int is_offsets, int unsafe, int64_t nrows,
-                        int64_t* spans, uint32_t* status, void* stream);
+ * Descriptor status bits, ORed into a caller-owned device word (never a device assert):
+ * 1 a length is negative or > nrows, 2 lengths do not cover nrows (checked unless unsafe),
+ * 4 a boundary lies outside [0, nrows], 8 boundaries decrease. The word is sticky: the library
+ * only sets bits, the caller clears it. */
 
-/* Ordered storage-dtype pooling (neptune_codegen/torch_op.py:254-306, launch
- * :390-410): for each segment s and channel c, acc = initial, then for every row r in
- * [spans[s], spans[s+1]) in order acc = round_storage(acc + data[r, c]); reduce 0 sum,
- * 1 mean = div_rn(acc, float(round_storage(count))). Empty mean without initial and
- * invalid spans give NaN. initial_bits is the fp32 bit pattern of `initial`.
- * out is contiguous [nsegments, channels]. */
+/* Span construction from lengths (neptune_codegen/torch_op.py:370-387: cat(0, cumsum(lengths))
+ * and its assertions): int64 spans[nsegments + 1] from lengths with element stride length_stride.
+ * Offsets need no construction: nb200_segment_pool reads them directly. */
+int nb200_segment_spans(const void* lengths, int index_dtype, int64_t nsegments, int64_t length_stride,
+                        int unsafe, int64_t nrows, int64_t* spans, uint32_t* status, void* stream);
+
+/* Ordered storage-dtype pooling (neptune_codegen/torch_op.py:254-306, launch :390-410): for each
+ * segment s and channel c, acc = initial, then for every row r in [bounds[s], bounds[s+1]) in order
+ * acc = round_storage(acc + data[r, c]); reduce 0 sum, 1 mean = div_rn(acc,
+ * float(round_storage(count))). Empty mean without initial and malformed boundaries give NaN.
+ * bounds are nsegments + 1 CSR boundaries (int32 or int64, element stride bound_stride), validated
+ * in the kernel into *status (nullable). initial_bits is the fp32 bit pattern of `initial`. out is
+ * contiguous [nsegments, channels]. */
 int nb200_segment_pool(const void* data, int dtype, int64_t nrows, int64_t channels,
                        int64_t stride_row, int64_t stride_channel,
-                       const int64_t* spans, int64_t nsegments, int reduce,
-                       int has_initial, uint32_t initial_bits, void* out, void* stream);
+                       const void* bounds, int index_dtype, int64_t bound_stride, int64_t nsegments,
+                       int reduce, int has_initial, uint32_t initial_bits, void* out,
+                       uint32_t* status, void* stream);
 
 /* ------------------------------------------------------------------ a9: attention
  * O = softmax(scale * Q K^T [+ causal mask]) V per (batch, head), bf16 in/out with

@@ -23,7 +23,7 @@ NB200_ERR_UNSUPPORTED = -5
 DTYPE_CODES = {"float32": 0, "bfloat16": 1, "float16": 2}
 INDEX_CODES = {"int32": 0, "int64": 1}
 
-VARIANT_AUTO, VARIANT_WARP_ROW, VARIANT_CTA_ROW = 0, 1, 2
+VARIANT_AUTO, VARIANT_WARP_ROW, VARIANT_CTA_ROW, VARIANT_STREAM = 0, 1, 2, 3
 
 
 class NB200Params(ctypes.Structure):
@@ -49,6 +49,7 @@ SIGNATURES = {
     "nb200_last_error": (ctypes.c_char_p, []),
     "nb200_version": (ctypes.c_char_p, []),
     "nb200_launch_count": (ctypes.c_uint64, []),
+    "nb200_stream_fault": (_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "nb200_fold": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _int, _i64, _i64, _i64, _i64, _vp,
                           ctypes.POINTER(NB200Launch), _vp]),
     "nb200_softmax": (_int, [_int, _vp, _int, _i64, _i64, _i64, _i64, _vp, _vp, ctypes.POINTER(NB200Launch), _vp]),
@@ -61,9 +62,9 @@ SIGNATURES = {
     "nb200_fold_merge": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
     "nb200_rms_norm": (_int, [_vp, _vp, _int, _i64, _i64, _i64, _i64, _i64, _dbl, _vp,
                               ctypes.POINTER(NB200Launch), _vp]),
-    "nb200_segment_spans": (_int, [_vp, _int, _i64, _i64, _int, _int, _i64, _vp, _vp, _vp]),
-    "nb200_segment_pool": (_int, [_vp, _int, _i64, _i64, _i64, _i64, _vp, _i64, _int, _int, ctypes.c_uint32,
-                                  _vp, _vp]),
+    "nb200_segment_spans": (_int, [_vp, _int, _i64, _i64, _int, _i64, _vp, _vp, _vp]),
+    "nb200_segment_pool": (_int, [_vp, _int, _i64, _i64, _i64, _i64, _vp, _int, _i64, _i64, _int, _int,
+                                  ctypes.c_uint32, _vp, _vp, _vp]),
     "nb200_attention": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _int, ctypes.c_float, _vp]),
 }
 
@@ -108,6 +109,13 @@ def last_error() -> str:
 def launch_count() -> int:
     """Kernel launches this process issued through the library (its own counter)."""
     return int(load().nb200_launch_count())
+
+
+def stream_fault() -> int:
+    """Read and clear the streaming kernels' fault bits (synchronous; 0 means no wait ran out)."""
+    bits = ctypes.c_uint32(0)
+    check(load().nb200_stream_fault(ctypes.byref(bits)), "nb200_stream_fault")
+    return int(bits.value)
 
 
 def check(rc: int, what: str) -> None:

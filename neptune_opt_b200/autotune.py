@@ -6,6 +6,9 @@ that policy and its vocabulary -- a `(block, num_warps)` pair, `(rows class, pow
 keys, a machine-keyed table holding only measured deviations from the default, a noise margin a
 candidate must clear -- but the pair now selects a CUDA launch:
 
+* ``num_warps == 0``: the library's own policy -- rows that are contiguous and 16-byte aligned are
+  staged through shared memory with bulk copies (each warp owns a ring of stages), others use the
+  register-tiled kernels below;
 * ``num_warps == 1``: one warp folds one row (persistent CTAs of 8 warps, row chunks resident in
   registers, no shared memory or barriers);
 * ``num_warps >= 2``: one CTA of ``32 * num_warps`` threads folds one row (cross-warp reduction
@@ -14,8 +17,7 @@ candidate must clear -- but the pair now selects a CUDA launch:
   their register tile from the row width themselves, so for the serial plan ``block`` only takes
   part in the operator's identity.
 
-The default depends on the row's byte width (rows up to 16 KB fit a warp's registers), which is why
-it is a function here rather than a constant.
+The default is the library's policy, `(SPLIT_BLOCK, 0)`.
 """
 from __future__ import annotations
 
@@ -27,6 +29,7 @@ from neptune_opt_b200._lib import VARIANT_CTA_ROW, VARIANT_WARP_ROW, launch_stru
 
 # Every configuration the search may choose from.
 CANDIDATES: tuple = (
+    (16384, 0),
     (4096, 1), (16384, 1),
     (4096, 4), (16384, 4),
     (4096, 8), (16384, 8),
@@ -89,10 +92,8 @@ def _elem_bytes(dtype) -> int:
 
 
 def default_config(ncols=None, dtype=None) -> tuple:
-    """Warp per row while the row fits 16 KB, else a CTA of 8 warps per row."""
-    if not isinstance(ncols, int):
-        return (SPLIT_BLOCK, 1)
-    return (SPLIT_BLOCK, 1) if ncols * _elem_bytes(dtype) <= WARP_ROW_BYTES else (SPLIT_BLOCK, 8)
+    """The library's launch policy (bulk-copy staging when eligible)."""
+    return (SPLIT_BLOCK, 0)
 
 
 DEFAULT = default_config()
@@ -126,6 +127,21 @@ def table(machine: str | None = None) -> dict:
     return dict(all_tables.get(machine, {}).get("table", {}))
 
 
+_NAMES: dict = {}
+
+
+def _device_name(device: str):
+    """The GPU name of a CUDA device string, cached (asked once per device)."""
+    if device not in _NAMES:
+        try:
+            import torch
+
+            _NAMES[device] = torch.cuda.get_device_name(torch.device(device))
+        except Exception:  # noqa: BLE001
+            _NAMES[device] = None
+    return _NAMES[device]
+
+
 def best_config(rows, ncols, dtype=None, device=None, device_name=None, verbose: bool = False) -> tuple:
     """`(block, num_warps)` for a shape on this machine: measured entry, else the default."""
     if not isinstance(rows, int) or not isinstance(ncols, int):
@@ -134,12 +150,7 @@ def best_config(rows, ncols, dtype=None, device=None, device_name=None, verbose:
     if device is not None and str(device).split(":", 1)[0] != "cuda":
         return default
     if device_name is None and device is not None:
-        try:
-            import torch
-
-            device_name = torch.cuda.get_device_name(torch.device(device))
-        except Exception:  # noqa: BLE001
-            device_name = None
+        device_name = _device_name(str(device))
     machine = machine_key(device_name) if device_name else ""
     cfg = table(machine).get(shape_key(rows, ncols), default) if machine else default
     if verbose:
@@ -152,7 +163,7 @@ def launch_for(cfg) -> object | None:
     if cfg is None:
         return None
     _block, warps = cfg
-    if warps is None:
+    if not warps:
         return None
     if warps <= 1:
         return launch_struct(VARIANT_WARP_ROW, 0, 0)

@@ -103,7 +103,7 @@ int check_rows(const void* x, int dtype, int64_t rows, int64_t ncols, const void
 
 int check_launch(const nb200_launch* L) {
     if (!L) return NB200_OK;
-    if (L->variant < 0 || L->variant > NB200_VARIANT_CTA_ROW) { set_error("unknown launch variant %d", L->variant); return NB200_ERR_ARG; }
+    if (L->variant < 0 || L->variant > NB200_VARIANT_STREAM) { set_error("unknown launch variant %d", L->variant); return NB200_ERR_ARG; }
     if (L->threads && (L->threads < 64 || L->threads > 512 || L->threads % 32)) {
         set_error("launch threads must be a multiple of 32 in [64, 512]"); return NB200_ERR_ARG;
     }
@@ -118,6 +118,14 @@ extern "C" {
 const char* nb200_last_error(void) { return g_error; }
 const char* nb200_version(void) { return "neptune_b200 0.1 (sm_100a)"; }
 uint64_t nb200_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int nb200_stream_fault(uint32_t* bits) {
+    if (!bits) { set_error("nb200_stream_fault: null pointer"); return NB200_ERR_ARG; }
+    unsigned int v = 0;
+    const int rc = stream_fault_take(&v);
+    *bits = v;
+    return rc;
+}
 
 int nb200_fold(int skeleton, const nb200_params* params, const void* x, int dtype, int64_t rows,
                int64_t ncols, int64_t stride_row, int64_t stride_col, void* out,
@@ -236,30 +244,32 @@ int nb200_rms_norm(const void* x, const void* gamma, int dtype, int64_t rows, in
                       launch, (cudaStream_t)stream);
 }
 
-int nb200_segment_spans(const void* segments, int index_dtype, int64_t nsegments, int64_t seg_stride,
-                        int is_offsets, int unsafe, int64_t nrows, int64_t* spans, uint32_t* status,
-                        void* stream) {
+int nb200_segment_spans(const void* lengths, int index_dtype, int64_t nsegments, int64_t length_stride,
+                        int unsafe, int64_t nrows, int64_t* spans, uint32_t* status, void* stream) {
     if (index_dtype != NB200_I32 && index_dtype != NB200_I64) {
         set_error("segment index dtype must be int32/int64"); return NB200_ERR_ARG;
     }
     if (nsegments < 0 || nrows < 0) { set_error("nb200_segment_spans: negative size"); return NB200_ERR_ARG; }
-    if (!spans || !status || ((nsegments > 0 || is_offsets) && !segments)) {
-        set_error("nb200_segment_spans: null pointer"); return NB200_ERR_ARG;
-    }
-    return launch_spans(segments, index_dtype, nsegments, seg_stride, is_offsets, unsafe, nrows, spans,
-                        status, (cudaStream_t)stream);
+    if (!spans || (nsegments > 0 && !lengths)) { set_error("nb200_segment_spans: null pointer"); return NB200_ERR_ARG; }
+    return launch_spans(lengths, index_dtype, nsegments, length_stride, unsafe, nrows, spans, status,
+                        (cudaStream_t)stream);
 }
 
 int nb200_segment_pool(const void* data, int dtype, int64_t nrows, int64_t channels, int64_t stride_row,
-                       int64_t stride_channel, const int64_t* spans, int64_t nsegments, int reduce,
-                       int has_initial, uint32_t initial_bits, void* out, void* stream) {
+                       int64_t stride_channel, const void* bounds, int index_dtype, int64_t bound_stride,
+                       int64_t nsegments, int reduce, int has_initial, uint32_t initial_bits, void* out,
+                       uint32_t* status, void* stream) {
     if (!valid_dtype(dtype)) { set_error("segment data dtype must be float16/bfloat16/float32"); return NB200_ERR_ARG; }
+    if (index_dtype != NB200_I32 && index_dtype != NB200_I64) {
+        set_error("segment index dtype must be int32/int64"); return NB200_ERR_ARG;
+    }
     if (reduce != 0 && reduce != 1) { set_error("segment reduce must be 0 (sum) or 1 (mean)"); return NB200_ERR_ARG; }
     if (nrows < 0 || channels < 0 || nsegments < 0) { set_error("nb200_segment_pool: negative size"); return NB200_ERR_ARG; }
     if (nsegments == 0 || channels == 0) return NB200_OK;
-    if (!spans || !out || (nrows > 0 && !data)) { set_error("nb200_segment_pool: null pointer"); return NB200_ERR_ARG; }
-    return launch_segment_pool(data, dtype, nrows, channels, stride_row, stride_channel, spans, nsegments,
-                               reduce, has_initial, initial_bits, out, (cudaStream_t)stream);
+    if (!bounds || !out || (nrows > 0 && !data)) { set_error("nb200_segment_pool: null pointer"); return NB200_ERR_ARG; }
+    return launch_segment_pool(data, dtype, nrows, channels, stride_row, stride_channel, bounds, index_dtype,
+                               bound_stride, nsegments, reduce, has_initial, initial_bits, out, status,
+                               (cudaStream_t)stream);
 }
 
 int nb200_attention(const void* q, const void* k, const void* v, void* o, float* lse, int64_t batch,

@@ -47,11 +47,19 @@ template <> struct Sk<NB200_SOFTCAP_LSE> {
 
 // ---- max|c| producer, sum consumer. `floor` marks the zero-singular coordinate that the
 // reference floors at 1e-30 on both repair endpoints (algebra.py:329-345).
+// term(v, den) is the consumer term; prep(den) and term_r(v, c) give the same term with the
+// per-chunk constant c = prep(den) hoisted out of the element loop (a reciprocal instead of a
+// division per element; the two differ by at most one rounding).
 template <> struct Sk<NB200_STABLE_L2> {
     static constexpr int kind = K_MAXABS;
     static constexpr bool floor = true;
     __device__ __forceinline__ static float term(float v, float den, const Params&) {
         const float r = v / den;
+        return r * r;
+    }
+    __device__ __forceinline__ static float prep(float den, const Params&) { return 1.0f / den; }
+    __device__ __forceinline__ static float term_r(float v, float c) {
+        const float r = v * c;
         return r * r;
     }
     __device__ __forceinline__ static float factor(float q, float qn, const Params&) {
@@ -66,6 +74,8 @@ template <> struct Sk<NB200_LINEAR_ATTN> {
     static constexpr int kind = K_MAXABS;
     static constexpr bool floor = true;
     __device__ __forceinline__ static float term(float v, float den, const Params&) { return v / den; }
+    __device__ __forceinline__ static float prep(float den, const Params&) { return 1.0f / den; }
+    __device__ __forceinline__ static float term_r(float v, float c) { return v * c; }
     __device__ __forceinline__ static float factor(float q, float qn, const Params&) { return q / qn; }
     __device__ __forceinline__ static float fin(float, float acc, const Params&) { return acc; }
 };
@@ -73,6 +83,8 @@ template <> struct Sk<NB200_DECAY_RENORM> {
     static constexpr int kind = K_MAXABS;
     static constexpr bool floor = false;
     __device__ __forceinline__ static float term(float v, float den, const Params& p) { return v / (den + p.N); }
+    __device__ __forceinline__ static float prep(float den, const Params& p) { return 1.0f / (den + p.N); }
+    __device__ __forceinline__ static float term_r(float v, float c) { return v * c; }
     __device__ __forceinline__ static float factor(float q, float qn, const Params& p) {
         return (q + p.N) / (qn + p.N);
     }
@@ -84,6 +96,8 @@ template <> struct Sk<NB200_SUMSQ_DIV> {
     __device__ __forceinline__ static float term(float v, float den, const Params&) {
         return (v * v) * (1.0f / den);
     }
+    __device__ __forceinline__ static float prep(float den, const Params&) { return 1.0f / den; }
+    __device__ __forceinline__ static float term_r(float v, float c) { return (v * v) * c; }
     __device__ __forceinline__ static float factor(float q, float qn, const Params&) { return q / qn; }
     __device__ __forceinline__ static float fin(float, float acc, const Params&) { return acc; }
 };

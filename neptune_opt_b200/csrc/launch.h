@@ -28,11 +28,26 @@ int launch_rms(const void* x, const void* gamma, int dtype, int64_t rows, int64_
                int64_t srow, int64_t scol, int64_t sg, float eps, void* out,
                const nb200_launch* L, cudaStream_t st);
 
-int launch_spans(const void* seg, int idt, int64_t nseg, int64_t sstride, int is_offsets,
-                 int unsafe, int64_t nrows, int64_t* spans, uint32_t* status, cudaStream_t st);
-int launch_segment_pool(const void* data, int dtype, int64_t nrows, int64_t channels,
-                        int64_t srow, int64_t sch, const int64_t* spans, int64_t nseg, int reduce,
-                        int has_initial, uint32_t initial_bits, void* out, cudaStream_t st);
+int launch_spans(const void* seg, int idt, int64_t nseg, int64_t sstride, int unsafe, int64_t nrows,
+                 int64_t* spans, uint32_t* status, cudaStream_t st);
+int launch_segment_pool(const void* data, int dtype, int64_t nrows, int64_t channels, int64_t srow, int64_t sch,
+                        const void* bounds, int idt, int64_t bs, int64_t nseg, int reduce, int has_initial,
+                        uint32_t initial_bits, void* out, uint32_t* status, cudaStream_t st);
+
+// Streaming (bulk-copy staged) paths: return 1 when launched, 0 when the input is not eligible
+// (the caller then uses the register-tiled kernels), negative on error.
+int stream_fold(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow,
+                int64_t scol, void* out, cudaStream_t st);
+int stream_softmax(int mode, const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
+                   void* y, void* lse, cudaStream_t st);
+int stream_l2(const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol, void* y, void* norm,
+              cudaStream_t st);
+int stream_rms(const void* x, const void* gamma, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
+               int64_t sg, float eps, void* y, cudaStream_t st);
+int stream_span(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t cb, int64_t ns,
+                int64_t srow, int64_t scol, int64_t cc, int64_t nparts, nb200_state* states, void* out,
+                int finalize, cudaStream_t st);
+int stream_fault_take(unsigned int* bits);
 
 int launch_attention(const void* q, const void* k, const void* v, void* o, float* lse,
                      int64_t B, int64_t H, int64_t S, int64_t D, int causal, float scale,

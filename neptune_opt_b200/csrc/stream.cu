@@ -1,0 +1,615 @@
+// Streaming (bulk-copy staged) kernels for contiguous, 16-byte-aligned rows on sm_100a.
+//
+// rows_kernel: every warp owns a ring of S shared-memory stages, each holding R whole rows. Lane 0
+// refills a stage with cp.async.bulk as soon as the warp has read it, so S-1 stages per warp are
+// in flight while the warp computes on the third; the row is read from HBM exactly once and every
+// further pass (max, sum, readout) reads shared memory. One Op per fused region:
+//   FoldOp    the serial repaired fold of any skeleton (template.py:41-54, two-pass :62-103)
+//   SoftmaxOp softmax / log_softmax + logsumexp (the lowering of neptune_recognize/lowering.py:80-99)
+//   L2Op      stable_l2 norm and x / norm
+//   RmsOp     RMSNorm with the reference's fp32 stages (emitters.py:576-595)
+// span_kernel: every warp folds a contiguous column span of one row (a split-plan chunk, or a whole
+// row too wide for one stage) through its ring in sub-blocks, keeping a per-lane fold state; at the
+// span's end the 32 lane states merge in a fixed tree and the warp writes the chunk state (split
+// plan, template.py:137-165) or the finalised result.
+#include <algorithm>
+
+#include "launch.h"
+#include "stream.cuh"
+
+namespace nb200 {
+
+struct RowPlan {
+    int64_t rows, ncols, srow;  // srow in elements
+    int64_t nblocks;            // ceil(rows / R)
+    uint32_t row_bytes, stage_bytes, extra_bytes, bar_offset, stage_offset;
+    int R, S, packed;
+};
+
+// ------------------------------------------------------------------ packed arithmetic helpers
+__device__ __forceinline__ unsigned long long pk(float a, float b) {
+    return (static_cast<unsigned long long>(__float_as_uint(b)) << 32) | __float_as_uint(a);
+}
+__device__ __forceinline__ float lo_f(unsigned long long v) { return __uint_as_float(static_cast<uint32_t>(v)); }
+__device__ __forceinline__ float hi_f(unsigned long long v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
+__device__ __forceinline__ unsigned long long mul_f32x2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long add_f32x2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// Two storage values of one 32-bit word as fp32 (low half first).
+template <typename T> struct Word;
+template <> struct Word<__nv_bfloat16> {
+    __device__ __forceinline__ static unsigned long long unpack(uint32_t w) {
+        return pk(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+    }
+    // RN(a * g) of bf16 pairs: the product of two bf16 values is exact in fp32, so this is the
+    // reference's fp32 product rounded to bf16.
+    __device__ __forceinline__ static uint32_t round_pair(unsigned long long v) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(lo_f(v), hi_f(v));
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+    __device__ __forceinline__ static uint32_t mul_pair(uint32_t a, uint32_t g) {
+        uint32_t d;
+        asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(g));
+        return d;
+    }
+};
+template <> struct Word<__half> {
+    __device__ __forceinline__ static unsigned long long unpack(uint32_t w) {
+        __half2 h = *reinterpret_cast<__half2*>(&w);
+        float2 f = __half22float2(h);
+        return pk(f.x, f.y);
+    }
+    __device__ __forceinline__ static uint32_t round_pair(unsigned long long v) {
+        __half2 h = __floats2half2_rn(lo_f(v), hi_f(v));
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+    __device__ __forceinline__ static uint32_t mul_pair(uint32_t a, uint32_t g) {
+        uint32_t d;
+        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(g));
+        return d;
+    }
+};
+
+__device__ __forceinline__ uint32_t word(const uint4& u, int i) {
+    return i == 0 ? u.x : i == 1 ? u.y : i == 2 ? u.z : u.w;
+}
+
+// ------------------------------------------------------------------ Ops
+template <int S, typename T>
+struct FoldOp {
+    T* out;
+    Params p;
+    int nv;
+    __device__ __forceinline__ void prologue(unsigned char*) const {}
+    __device__ __forceinline__ void row(const uint4* v, int64_t r, int lane, const unsigned char*) const {
+        float res;
+        if constexpr (Sk<S>::kind == K_TWOPASS) {
+            constexpr int V = Elem<T>::V;
+            float sv[V], av[V];
+#pragma unroll
+            for (int e = 0; e < V; ++e) { sv[e] = 0.f; av[e] = 0.f; }
+            for (int j = lane; j < nv; j += 32) {
+                const uint4 u = v[j];
+#pragma unroll
+                for (int e = 0; e < V; ++e) sv[e] += Elem<T>::lane(u, e) * p.invN;
+            }
+            const float mean = warp_sum(combine_sum<V>(sv));
+            for (int j = lane; j < nv; j += 32) {
+                const uint4 u = v[j];
+#pragma unroll
+                for (int e = 0; e < V; ++e) {
+                    const float d = Elem<T>::lane(u, e) - mean;
+                    av[e] += p.invN * (d * d);
+                }
+            }
+            res = Sk<S>::fin(warp_sum(combine_sum<V>(av)));
+        } else {
+            const St s = warp_merge<S>(lane_state<S, T>(v, nv, lane, p), lane, p);
+            res = finalize<S>(s, p);
+        }
+        if (lane == 0) out[r] = Elem<T>::from_f(res);
+    }
+};
+
+template <typename T>
+struct SoftmaxOp {
+    T* y;
+    T* lse;
+    int64_t ncols;
+    int nv, mode;
+    __device__ __forceinline__ void prologue(unsigned char*) const {}
+    __device__ __forceinline__ void row(const uint4* v, int64_t r, int lane, const unsigned char*) const {
+        constexpr int V = Elem<T>::V;
+        const Params p{0.f, 0.f, 1.f, 1.f, 0.f, 0.f, 0.f};
+        const St s = warp_merge<NB200_LOGSUMEXP>(lane_state<NB200_LOGSUMEXP, T>(v, nv, lane, p), lane, p);
+        const bool bad = s.status != 0 || !s.seen;
+        const float m = s.m, inv = 1.0f / s.acc, lg = logf(s.acc);
+        T* yrow = y + r * ncols;
+        for (int j = lane; j < nv; j += 32) {
+            const uint4 u = v[j];
+            float f[V];
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+                const float d = Elem<T>::lane(u, e) - m;
+                f[e] = bad ? NB200_NAN : (mode == 0 ? fexp(d) * inv : d - lg);
+            }
+            st_stream(yrow + (int64_t)j * V, Elem<T>::pack(f));
+        }
+        if (lse != nullptr && lane == 0) lse[r] = Elem<T>::from_f(finalize<NB200_LOGSUMEXP>(s, p));
+    }
+};
+
+template <typename T>
+struct L2Op {
+    T* y;
+    T* norm;
+    int64_t ncols;
+    int nv;
+    __device__ __forceinline__ void prologue(unsigned char*) const {}
+    __device__ __forceinline__ void row(const uint4* v, int64_t r, int lane, const unsigned char*) const {
+        constexpr int V = Elem<T>::V;
+        const Params p{0.f, 0.f, 1.f, 1.f, 0.f, 0.f, 0.f};
+        const St s = warp_merge<NB200_STABLE_L2>(lane_state<NB200_STABLE_L2, T>(v, nv, lane, p), lane, p);
+        const float nrm = finalize<NB200_STABLE_L2>(s, p);
+        const float inv = 1.0f / nrm;
+        T* yrow = y + r * ncols;
+        for (int j = lane; j < nv; j += 32) {
+            const uint4 u = v[j];
+            float f[V];
+#pragma unroll
+            for (int e = 0; e < V; ++e) f[e] = Elem<T>::lane(u, e) * inv;
+            st_stream(yrow + (int64_t)j * V, Elem<T>::pack(f));
+        }
+        if (norm != nullptr && lane == 0) norm[r] = Elem<T>::from_f(nrm);
+    }
+};
+
+// gamma (ncols values) is staged once per CTA at the start of shared memory.
+template <typename T>
+struct RmsOp {
+    T* y;
+    const T* gamma;
+    int64_t ncols, sg;
+    int nv;
+    float eps, count;
+    __device__ __forceinline__ void prologue(unsigned char* smem) const {
+        T* g = reinterpret_cast<T*>(smem);
+        for (int64_t c = threadIdx.x; c < ncols; c += blockDim.x) g[c] = gamma[c * sg];
+    }
+    __device__ __forceinline__ void row(const uint4* v, int64_t r, int lane, const unsigned char* smem) const {
+        constexpr int V = Elem<T>::V;
+        const uint4* g = reinterpret_cast<const uint4*>(smem);
+        T* yrow = y + r * ncols;
+        if constexpr (sizeof(T) == 2) {
+            // sum of squares: every square and every add rounded (no contraction), two lanes of
+            // fp32 per instruction
+            unsigned long long acc[4] = {0ull, 0ull, 0ull, 0ull};
+            for (int j = lane; j < nv; j += 32) {
+                const uint4 u = v[j];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const unsigned long long f = Word<T>::unpack(word(u, i));
+                    acc[i] = add_f32x2(acc[i], mul_f32x2(f, f));
+                }
+            }
+            const unsigned long long a01 = add_f32x2(acc[0], acc[1]), a23 = add_f32x2(acc[2], acc[3]);
+            const unsigned long long a = add_f32x2(a01, a23);
+            const float total = warp_sum(__fadd_rn(lo_f(a), hi_f(a)));
+            const float mean = __fdiv_rn(total, count);
+            const float scale = __frsqrt_rn(__fadd_rn(mean, eps));
+            const unsigned long long sc = pk(scale, scale);
+            for (int j = lane; j < nv; j += 32) {
+                const uint4 u = v[j], gg = g[j];
+                uint4 o;
+                o.x = Word<T>::mul_pair(Word<T>::round_pair(mul_f32x2(Word<T>::unpack(u.x), sc)), gg.x);
+                o.y = Word<T>::mul_pair(Word<T>::round_pair(mul_f32x2(Word<T>::unpack(u.y), sc)), gg.y);
+                o.z = Word<T>::mul_pair(Word<T>::round_pair(mul_f32x2(Word<T>::unpack(u.z), sc)), gg.z);
+                o.w = Word<T>::mul_pair(Word<T>::round_pair(mul_f32x2(Word<T>::unpack(u.w), sc)), gg.w);
+                st_stream(yrow + (int64_t)j * V, o);
+            }
+        } else {
+            unsigned long long acc0 = 0ull, acc1 = 0ull;
+            for (int j = lane; j < nv; j += 32) {
+                const uint4 u = v[j];
+                const unsigned long long a = pk(__uint_as_float(u.x), __uint_as_float(u.y));
+                const unsigned long long b = pk(__uint_as_float(u.z), __uint_as_float(u.w));
+                acc0 = add_f32x2(acc0, mul_f32x2(a, a));
+                acc1 = add_f32x2(acc1, mul_f32x2(b, b));
+            }
+            const unsigned long long acc = add_f32x2(acc0, acc1);
+            const float total = warp_sum(__fadd_rn(lo_f(acc), hi_f(acc)));
+            const float mean = __fdiv_rn(total, count);
+            const float scale = __frsqrt_rn(__fadd_rn(mean, eps));
+            const unsigned long long sc = pk(scale, scale);
+            for (int j = lane; j < nv; j += 32) {
+                const uint4 u = v[j], gg = g[j];
+                const unsigned long long a = mul_f32x2(mul_f32x2(pk(__uint_as_float(u.x), __uint_as_float(u.y)), sc),
+                                                       pk(__uint_as_float(gg.x), __uint_as_float(gg.y)));
+                const unsigned long long b = mul_f32x2(mul_f32x2(pk(__uint_as_float(u.z), __uint_as_float(u.w)), sc),
+                                                       pk(__uint_as_float(gg.z), __uint_as_float(gg.w)));
+                st_stream(yrow + (int64_t)j * V, make_uint4(static_cast<uint32_t>(a), static_cast<uint32_t>(a >> 32),
+                                                            static_cast<uint32_t>(b), static_cast<uint32_t>(b >> 32)));
+            }
+        }
+    }
+};
+
+// ------------------------------------------------------------------ resident-row kernel
+template <typename T, class Op>
+__global__ void __launch_bounds__(256) rows_kernel(const T* __restrict__ x, RowPlan pl, Op op) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + pl.bar_offset) + warp * pl.S;
+    unsigned char* ring = smem + pl.stage_offset + (size_t)warp * pl.S * pl.stage_bytes;
+    op.prologue(smem);
+    if (lane == 0) {
+        for (int s = 0; s < pl.S; ++s) mbar_init(&bar[s], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const int64_t gw = (int64_t)blockIdx.x * nw + warp, GW = (int64_t)gridDim.x * nw;
+    auto issue = [&](int64_t b, int s) {
+        const int64_t r0 = b * pl.R;
+        const int nr = (int)min((int64_t)pl.R, pl.rows - r0);
+        unsigned char* dst = ring + (size_t)s * pl.stage_bytes;
+        mbar_expect_tx(&bar[s], (uint32_t)nr * pl.row_bytes);
+        if (pl.packed) {
+            bulk_load(dst, x + r0 * pl.srow, (uint32_t)nr * pl.row_bytes, &bar[s]);
+        } else {
+            for (int i = 0; i < nr; ++i) bulk_load(dst + (size_t)i * pl.row_bytes, x + (r0 + i) * pl.srow, pl.row_bytes, &bar[s]);
+        }
+    };
+    if (lane == 0)
+        for (int s = 0; s < pl.S; ++s)
+            if (gw + s * GW < pl.nblocks) issue(gw + s * GW, s);
+    __syncwarp();
+    int64_t k = 0;
+    for (int64_t b = gw; b < pl.nblocks; b += GW, ++k) {
+        const int s = (int)(k % pl.S);
+        const uint32_t parity = (uint32_t)((k / pl.S) & 1);
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar[s], parity))) {
+            // A wait ran out (fault bit already set): give the copies still in flight a bounded
+            // chance to land before the CTA's shared memory is released, then stop.
+            for (int64_t kk = k; kk < k + pl.S; ++kk)
+                if (gw + kk * GW < pl.nblocks) mbar_wait(&bar[kk % pl.S], (uint32_t)((kk / pl.S) & 1));
+            return;
+        }
+        const unsigned char* stage = ring + (size_t)s * pl.stage_bytes;
+        const int64_t r0 = b * pl.R;
+        const int nr = (int)min((int64_t)pl.R, pl.rows - r0);
+        for (int i = 0; i < nr; ++i)
+            op.row(reinterpret_cast<const uint4*>(stage + (size_t)i * pl.row_bytes), r0 + i, lane, smem);
+        __syncwarp();
+        if (lane == 0 && b + pl.S * GW < pl.nblocks) {
+            fence_proxy_async();
+            issue(b + pl.S * GW, s);
+        }
+        __syncwarp();
+    }
+}
+
+// ------------------------------------------------------------------ span kernel
+struct SpanPlan {
+    int64_t rows, srow, cb, ns, cc, nparts, nitems;  // items = rows * nparts
+    int64_t sub_cols;                                // columns per staged sub-block
+    int nsub;                                        // sub-blocks per item (upper bound)
+    int S;
+    uint32_t stage_bytes, bar_offset, stage_offset;
+    int finalize;                                    // 1: write out[r]; 0: write states[item]
+};
+
+template <int S_, typename T>
+__global__ void __launch_bounds__(256) span_kernel(const T* __restrict__ x, SpanPlan pl, Params p,
+                                                   nb200_state* __restrict__ states, T* __restrict__ out) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int V = Elem<T>::V;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + pl.bar_offset) + warp * pl.S;
+    unsigned char* ring = smem + pl.stage_offset + (size_t)warp * pl.S * pl.stage_bytes;
+    if (lane == 0) {
+        for (int s = 0; s < pl.S; ++s) mbar_init(&bar[s], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const int64_t gw = (int64_t)blockIdx.x * nw + warp, GW = (int64_t)gridDim.x * nw;
+    // Task cursors walk (item, sub-block) pairs of this warp: items gw, gw + GW, ..., nsub
+    // sub-blocks each. `next` is the task to issue, `cur` the task to consume; both advance by
+    // increments, so the loop does no integer division per task.
+    struct Cursor {
+        int64_t item, row, lo, hi;  // item index, its row and its column span
+        int sub;
+    };
+    auto start_item = [&](Cursor& c, int64_t item) {
+        c.item = item;
+        c.sub = 0;
+        if (item < pl.nitems) {
+            c.row = item / pl.nparts;
+            const int64_t part = item - c.row * pl.nparts;
+            c.lo = pl.cb + part * pl.cc;
+            c.hi = min(c.lo + pl.cc, pl.cb + pl.ns);
+        }
+    };
+    auto advance = [&](Cursor& c) {
+        if (++c.sub == pl.nsub) start_item(c, c.item + GW);
+    };
+    int stage_issue = 0, stage_use = 0;
+    uint32_t parity = 0;
+    auto issue = [&](const Cursor& c) {
+        const int64_t c0 = c.lo + (int64_t)c.sub * pl.sub_cols;
+        const int64_t c1 = max(c0, min(c0 + pl.sub_cols, c.hi));
+        const uint32_t bytes = (uint32_t)((c1 - c0) * (int64_t)sizeof(T));
+        uint64_t* b = &bar[stage_issue];
+        if (bytes == 0) {  // an empty tail sub-block: complete the phase without a copy
+            mbar_arrive(b);
+        } else {
+            mbar_expect_tx(b, bytes);
+            bulk_load(ring + (size_t)stage_issue * pl.stage_bytes, x + c.row * pl.srow + c0, bytes, b);
+        }
+        stage_issue = stage_issue + 1 == pl.S ? 0 : stage_issue + 1;
+    };
+    Cursor next, cur;
+    start_item(next, gw);
+    start_item(cur, gw);
+    if (lane == 0)
+        for (int s = 0; s < pl.S && next.item < pl.nitems; ++s) {
+            issue(next);
+            advance(next);
+        }
+    __syncwarp();
+    St run = empty_state();
+    while (cur.item < pl.nitems) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar[stage_use], parity))) {
+            // bounded drain of the copies still in flight, then stop
+            int s = stage_use;
+            uint32_t ph = parity;
+            for (int k = 0; k < pl.S; ++k) {
+                mbar_wait(&bar[s], ph);
+                if (++s == pl.S) { s = 0; ph ^= 1u; }
+            }
+            return;
+        }
+        const int64_t c0 = cur.lo + (int64_t)cur.sub * pl.sub_cols;
+        const int64_t c1 = max(c0, min(c0 + pl.sub_cols, cur.hi));
+        const int nv = (int)((c1 - c0) / V);
+        const St sub = lane_state<S_, T>(reinterpret_cast<const uint4*>(ring + (size_t)stage_use * pl.stage_bytes), nv,
+                                         lane, p);
+        run = merge_fast<S_>(run, sub, p);
+        __syncwarp();
+        if (lane == 0 && next.item < pl.nitems) {
+            fence_proxy_async();
+            issue(next);
+        }
+        if (next.item < pl.nitems) advance(next);
+        if (++stage_use == pl.S) {
+            stage_use = 0;
+            parity ^= 1u;
+        }
+        if (cur.sub == pl.nsub - 1) {  // the item's last sub-block
+            const St w = warp_merge<S_>(run, lane, p);
+            if (lane == 0) {
+                if (pl.finalize) out[cur.row] = Elem<T>::from_f(finalize<S_>(w, p));
+                else reinterpret_cast<float4*>(states)[cur.item] =
+                         make_float4(w.m, w.acc, __int_as_float(w.seen), __int_as_float(w.status));
+            }
+            run = empty_state();
+        }
+        advance(cur);
+        __syncwarp();
+    }
+}
+
+// ================================================================== host side
+namespace {
+
+constexpr int kStreamThreads = 256;
+constexpr uint32_t kSmemBudget = 224 * 1024;
+
+inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
+
+template <typename K>
+int ensure_smem(K kernel, uint32_t bytes) {
+    static_assert(sizeof(K) > 0, "");
+    if (bytes <= 48 * 1024) return NB200_OK;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("cannot reserve %u bytes of shared memory", bytes);
+        return NB200_ERR_LAUNCH;
+    }
+    return NB200_OK;
+}
+
+// Rows are eligible when each row is a 16-byte-aligned, 16-byte-multiple contiguous run.
+template <typename T>
+bool rows_streamable(const T* x, int64_t rows, int64_t ncols, int64_t srow, int64_t scol) {
+    const int64_t rb = ncols * (int64_t)sizeof(T);
+    return scol == 1 && aligned16(x) && rb % 16 == 0 && (rows <= 1 || (srow * (int64_t)sizeof(T)) % 16 == 0) &&
+           rb <= 32768;
+}
+
+bool make_row_plan(int64_t rows, int64_t ncols, int64_t srow, size_t esize, uint32_t extra, RowPlan& pl) {
+    pl.rows = rows;
+    pl.ncols = ncols;
+    pl.srow = srow;
+    pl.row_bytes = (uint32_t)(ncols * (int64_t)esize);
+    pl.packed = (rows <= 1 || srow == ncols) ? 1 : 0;
+    int R = (int)std::max<int64_t>(1, 8192 / pl.row_bytes);
+    if (!pl.packed) R = std::min(R, 4);
+    pl.R = R;
+    pl.stage_bytes = align_up((uint32_t)R * pl.row_bytes, 128);
+    pl.nblocks = (rows + R - 1) / R;
+    pl.extra_bytes = align_up(extra, 128);
+    const int nw = kStreamThreads / 32;
+    pl.bar_offset = pl.extra_bytes;
+    pl.stage_offset = align_up(pl.bar_offset + nw * 4 * 8, 128);
+    int S = (int)((kSmemBudget - pl.stage_offset) / ((uint32_t)nw * pl.stage_bytes));
+    S = std::min(S, 4);
+    if (S < 2) return false;
+    pl.S = S;
+    return true;
+}
+
+uint32_t row_smem(const RowPlan& pl) { return pl.stage_offset + (uint32_t)(kStreamThreads / 32) * pl.S * pl.stage_bytes; }
+
+template <typename T, class Op>
+int launch_rows(const T* x, const RowPlan& pl, const Op& op, cudaStream_t st, const char* what) {
+    auto k = rows_kernel<T, Op>;
+    const uint32_t smem = row_smem(pl);
+    int rc = ensure_smem(k, smem);
+    if (rc) return rc;
+    const int g = persistent_grid(k, kStreamThreads, smem, (pl.nblocks + 7) / 8, 0);
+    k<<<g, kStreamThreads, smem, st>>>(x, pl, op);
+    count_launch();
+    return finish_launch(what);
+}
+
+}  // namespace
+
+int stream_fault_take(unsigned int* bits) {
+    unsigned int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_stream_fault, sizeof(v)) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_stream_fault, &zero, sizeof(zero)) != cudaSuccess) {
+        set_error("cannot read the streaming fault word: %s", cudaGetErrorString(cudaGetLastError()));
+        return NB200_ERR_LAUNCH;
+    }
+    *bits = v;
+    return NB200_OK;
+}
+
+// Returns 1 (and launches) when the streaming path applies, 0 when the caller should use the
+// register-tiled kernels, negative on error.
+template <typename T>
+int stream_fold_t(int sk, const Params& p, const T* x, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
+                  T* out, cudaStream_t st) {
+    if (!rows_streamable(x, rows, ncols, srow, scol)) return 0;
+    RowPlan pl;
+    if (!make_row_plan(rows, ncols, srow, sizeof(T), 0, pl)) return 0;
+    const int nv = (int)(ncols / Elem<T>::V);
+    int rc;
+    switch (sk) {
+#define X(S) case S: rc = launch_rows(x, pl, FoldOp<S, T>{out, p, nv}, st, "nb200_fold"); break;
+        X(NB200_LOGSUMEXP) X(NB200_LSE_BIASED) X(NB200_LSE_SCALED) X(NB200_SOFTCAP_LSE) X(NB200_STABLE_L2)
+        X(NB200_LINEAR_ATTN) X(NB200_DECAY_RENORM) X(NB200_SUMSQ_DIV) X(NB200_RMSNORM_MAX) X(NB200_VARIANCE)
+        X(NB200_STD)
+#undef X
+        default: return 0;
+    }
+    return rc ? rc : 1;
+}
+
+template <typename T>
+int stream_softmax_t(int mode, const T* x, int64_t rows, int64_t ncols, int64_t srow, int64_t scol, T* y, T* lse,
+                     cudaStream_t st) {
+    if (!rows_streamable(x, rows, ncols, srow, scol) || !aligned16(y)) return 0;
+    RowPlan pl;
+    if (!make_row_plan(rows, ncols, srow, sizeof(T), 0, pl)) return 0;
+    const int rc = launch_rows(x, pl, SoftmaxOp<T>{y, lse, ncols, (int)(ncols / Elem<T>::V), mode}, st, "nb200_softmax");
+    return rc ? rc : 1;
+}
+
+template <typename T>
+int stream_l2_t(const T* x, int64_t rows, int64_t ncols, int64_t srow, int64_t scol, T* y, T* norm, cudaStream_t st) {
+    if (!rows_streamable(x, rows, ncols, srow, scol) || !aligned16(y)) return 0;
+    RowPlan pl;
+    if (!make_row_plan(rows, ncols, srow, sizeof(T), 0, pl)) return 0;
+    const int rc = launch_rows(x, pl, L2Op<T>{y, norm, ncols, (int)(ncols / Elem<T>::V)}, st, "nb200_l2_normalize");
+    return rc ? rc : 1;
+}
+
+template <typename T>
+int stream_rms_t(const T* x, const T* gamma, int64_t rows, int64_t ncols, int64_t srow, int64_t scol, int64_t sg,
+                 float eps, T* y, cudaStream_t st) {
+    if (!rows_streamable(x, rows, ncols, srow, scol) || !aligned16(y)) return 0;
+    RowPlan pl;
+    if (!make_row_plan(rows, ncols, srow, sizeof(T), (uint32_t)(ncols * (int64_t)sizeof(T)), pl)) return 0;
+    const RmsOp<T> op{y, gamma, ncols, sg, (int)(ncols / Elem<T>::V), eps, static_cast<float>(ncols)};
+    const int rc = launch_rows(x, pl, op, st, "nb200_rms_norm");
+    return rc ? rc : 1;
+}
+
+// Column spans [cb + part * cc, ...) of every row, staged through 8 KB sub-blocks. finalize = 1
+// requires nparts == 1 (a whole row per item) and writes out[rows].
+template <typename T>
+int stream_span_t(int sk, const Params& p, const T* x, int64_t rows, int64_t cb, int64_t ns, int64_t srow,
+                  int64_t scol, int64_t cc, int64_t nparts, nb200_state* states, T* out, int finalize,
+                  cudaStream_t st) {
+    constexpr int V = Elem<T>::V;
+    if (scol != 1 || !aligned16(x) || (rows > 1 && (srow * (int64_t)sizeof(T)) % 16 != 0) || cb % V || ns % V ||
+        cc % V)
+        return 0;
+    if (sk == NB200_VARIANCE || sk == NB200_STD) return 0;
+    SpanPlan pl;
+    pl.rows = rows;
+    pl.srow = srow;
+    pl.cb = cb;
+    pl.ns = ns;
+    pl.cc = cc;
+    pl.nparts = nparts;
+    pl.nitems = rows * nparts;
+    pl.sub_cols = 8192 / (int64_t)sizeof(T);
+    pl.nsub = (int)((cc + pl.sub_cols - 1) / pl.sub_cols);
+    pl.stage_bytes = 8192;
+    pl.bar_offset = 0;
+    const int nw = kStreamThreads / 32;
+    pl.stage_offset = align_up(nw * 4 * 8, 128);
+    pl.S = 3;
+    pl.finalize = finalize;
+    const uint32_t smem = pl.stage_offset + (uint32_t)nw * pl.S * pl.stage_bytes;
+    int rc = NB200_OK;
+    auto go = [&](auto k) {
+        rc = ensure_smem(k, smem);
+        if (rc) return;
+        const int g = persistent_grid(k, kStreamThreads, smem, (pl.nitems + nw - 1) / nw, 0);
+        k<<<g, kStreamThreads, smem, st>>>(x, pl, p, states, out);
+        count_launch();
+        rc = finish_launch(finalize ? "nb200_fold" : "nb200_fold_partial");
+    };
+    switch (sk) {
+#define X(S) case S: go(span_kernel<S, T>); break;
+        X(NB200_LOGSUMEXP) X(NB200_LSE_BIASED) X(NB200_LSE_SCALED) X(NB200_SOFTCAP_LSE) X(NB200_STABLE_L2)
+        X(NB200_LINEAR_ATTN) X(NB200_DECAY_RENORM) X(NB200_SUMSQ_DIV) X(NB200_RMSNORM_MAX)
+#undef X
+        default: return 0;
+    }
+    return rc ? rc : 1;
+}
+
+#define NB200_STREAM_DTYPES(dtype, CALL)                            \
+    switch (dtype) {                                                \
+        case NB200_F32: { using T = float; return CALL; }           \
+        case NB200_BF16: { using T = __nv_bfloat16; return CALL; }  \
+        case NB200_F16: { using T = __half; return CALL; }          \
+    }                                                               \
+    return 0;
+
+int stream_fold(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow,
+                int64_t scol, void* out, cudaStream_t st) {
+    NB200_STREAM_DTYPES(dtype, stream_fold_t<T>(sk, p, (const T*)x, rows, ncols, srow, scol, (T*)out, st))
+}
+int stream_softmax(int mode, const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
+                   void* y, void* lse, cudaStream_t st) {
+    NB200_STREAM_DTYPES(dtype, stream_softmax_t<T>(mode, (const T*)x, rows, ncols, srow, scol, (T*)y, (T*)lse, st))
+}
+int stream_l2(const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol, void* y, void* norm,
+              cudaStream_t st) {
+    NB200_STREAM_DTYPES(dtype, stream_l2_t<T>((const T*)x, rows, ncols, srow, scol, (T*)y, (T*)norm, st))
+}
+int stream_rms(const void* x, const void* gamma, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
+               int64_t sg, float eps, void* y, cudaStream_t st) {
+    NB200_STREAM_DTYPES(dtype, stream_rms_t<T>((const T*)x, (const T*)gamma, rows, ncols, srow, scol, sg, eps, (T*)y, st))
+}
+int stream_span(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t cb, int64_t ns,
+                int64_t srow, int64_t scol, int64_t cc, int64_t nparts, nb200_state* states, void* out,
+                int finalize, cudaStream_t st) {
+    NB200_STREAM_DTYPES(dtype, stream_span_t<T>(sk, p, (const T*)x, rows, cb, ns, srow, scol, cc, nparts, states,
+                                                (T*)out, finalize, st))
+}
+
+}  // namespace nb200

@@ -68,8 +68,15 @@ def _is_metadata(x) -> bool:
     return isinstance(x, FakeTensor) or x.device.type == "meta"
 
 
+_DTYPE_CODES: dict = {}
+
+
 def dtype_code(dtype) -> int:
-    return _lib.DTYPE_CODES[str(dtype).removeprefix("torch.")]
+    code = _DTYPE_CODES.get(dtype)
+    if code is None:
+        code = _lib.DTYPE_CODES[str(dtype).removeprefix("torch.")]
+        _DTYPE_CODES[dtype] = code
+    return code
 
 
 def current_stream(device) -> int:
@@ -78,31 +85,28 @@ def current_stream(device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-class _on_device:
-    """Make `device` current for the duration of a launch (the stream belongs to it)."""
-
-    def __init__(self, device):
-        import torch
-
-        self.torch = torch
-        self.index = device.index if device.index is not None else torch.cuda.current_device()
-        self.prev = None
-
+class _NoGuard:
     def __enter__(self):
-        cur = self.torch.cuda.current_device()
-        if cur != self.index:
-            self.prev = cur
-            self.torch.cuda.set_device(self.index)
         return self
 
     def __exit__(self, *exc):
-        if self.prev is not None:
-            self.torch.cuda.set_device(self.prev)
         return False
 
 
-def _ptr(t) -> ctypes.c_void_p:
-    return ctypes.c_void_p(t.data_ptr())
+_NO_GUARD = _NoGuard()
+
+
+def _on_device(device):
+    """Make `device` current for a launch (its stream belongs to it); free when it already is."""
+    import torch
+
+    if device.index is None or device.index == torch.cuda.current_device():
+        return _NO_GUARD
+    return torch.cuda.device(device.index)
+
+
+def _ptr(t) -> int:
+    return t.data_ptr()
 
 
 def launch_reduction(name, plan, x2, out, rows, ncols, block=None, num_warps=None, params=None):

@@ -12,10 +12,10 @@ Differences from the reference, by design:
 * the ops are `torch.library.custom_op`s around C ABI launches instead of `triton_op`s;
   `as_triton_op`, `triton_op_name` and `_TRITON_OPS` remain as aliases of the CUDA names so the
   reference's callers keep working;
-* descriptor validation of segment pooling never traps the GPU: the span kernel records violations
-  in a status word and malformed spans pool to NaN (as the reference kernel itself does). Setting
-  NEPTUNE_B200_SYNC_CHECKS=1 (or calling `check_segment_status`) reads the status and raises the
-  reference's RuntimeError messages.
+* descriptor validation of segment pooling never traps the GPU: the kernels OR violations into a
+  sticky per-device status word and malformed spans pool to NaN (as the reference kernel itself
+  does). `segment_status()` reads and clears the word; with NEPTUNE_B200_SYNC_CHECKS=1 every call
+  checks it and raises the reference's RuntimeError messages.
 """
 from __future__ import annotations
 
@@ -259,6 +259,34 @@ def _sync_checks() -> bool:
     return os.environ.get("NEPTUNE_B200_SYNC_CHECKS", "") not in ("", "0")
 
 
+_STATUS: dict = {}
+
+
+def segment_status_word(device):
+    """The device's sticky descriptor-status word (int32, zero until a violation is recorded)."""
+    import torch
+
+    key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
+    word = _STATUS.get(key)
+    if word is None:
+        word = torch.zeros(1, dtype=torch.int32, device=device)
+        _STATUS[key] = word
+    return word
+
+
+def segment_status(device=None, clear: bool = True) -> int:
+    """Read (and by default clear) the descriptor-status bits recorded on `device` since the last
+    clear: 1 length negative or > nrows, 2 lengths do not cover nrows, 4 boundary out of
+    [0, nrows], 8 boundaries decreasing. Synchronises with the device."""
+    import torch
+
+    word = segment_status_word(torch.device("cuda", torch.cuda.current_device()) if device is None else device)
+    bits = int(word.item())
+    if clear and bits:
+        word.zero_()
+    return bits
+
+
 def check_segment_status(status) -> None:
     """Raise the reference's RuntimeError for the first violated descriptor condition."""
     bits = int(status.item()) if hasattr(status, "item") else int(status)
@@ -267,53 +295,57 @@ def check_segment_status(status) -> None:
             raise RuntimeError(message)
 
 
-def _segment_spans(data, segments, *, offsets, unsafe):
-    """int64 spans[nsegments + 1] and a device status word (torch_op.py:370-387)."""
+def _index_code(t) -> int:
+    return _lib.INDEX_CODES[str(t.dtype).removeprefix("torch.")]
+
+
+def _segment_bounds(data, segments, *, offsets, unsafe, status):
+    """(bounds tensor, index code, element stride) for the pooling kernel.
+
+    Offsets are read by the pooling kernel as they are (any int32/int64 stride), which also validates
+    them. Lengths become int64 spans cat(0, cumsum(lengths)) in one kernel that validates them
+    (torch_op.py:370-387)."""
     import torch
 
-    nrows = data.shape[0]
-    nseg = segments.shape[0] - 1 if offsets else segments.shape[0]
-    spans = torch.empty(max(nseg, 0) + 1, dtype=torch.int64, device=data.device)
-    status = torch.empty(1, dtype=torch.int32, device=data.device)
+    if offsets:
+        return segments, _index_code(segments), segments.stride(0) if segments.numel() else 1
+    nseg = segments.shape[0]
+    spans = torch.empty(nseg + 1, dtype=torch.int64, device=data.device)
     lib = _lib.load()
     with _on_device(data.device):
-        rc = lib.nb200_segment_spans(_ptr(segments), _lib.INDEX_CODES[str(segments.dtype).removeprefix("torch.")],
-                                     nseg, segments.stride(0) if segments.numel() else 1, int(offsets),
-                                     int(unsafe), nrows, _ptr(spans), _ptr(status),
-                                     ctypes.c_void_p(current_stream(data.device)))
+        rc = lib.nb200_segment_spans(_ptr(segments), _index_code(segments), nseg,
+                                     segments.stride(0) if segments.numel() else 1, int(unsafe), data.shape[0],
+                                     _ptr(spans), _ptr(status), ctypes.c_void_p(current_stream(data.device)))
     _lib.check(rc, "neptune segment spans")
-    if _sync_checks():
-        check_segment_status(status)
-    return spans, status
-
-
-LAST_SEGMENT_STATUS = None
+    return spans, _lib.INDEX_CODES["int64"], 1
 
 
 def _launch_segment(name, data, segments, params, plan):
-    """torch_op.py:390-410: spans, fresh output, one pooling launch."""
+    """torch_op.py:390-410: boundaries, fresh output, one pooling launch (plus one span launch for
+    lengths)."""
     import torch
 
-    global LAST_SEGMENT_STATUS
     shape = validate_segment_inputs(data, segments, reduce=name.removeprefix("segment_"), plan=plan, **params)
-    spans, status = _segment_spans(data, segments, offsets=params["offsets"], unsafe=params["unsafe"])
-    LAST_SEGMENT_STATUS = status
+    status = segment_status_word(data.device)
+    bounds, idx, bstride = _segment_bounds(data, segments, offsets=params["offsets"], unsafe=params["unsafe"],
+                                           status=status)
     channels = 1
     for size in data.shape[1:]:
         channels = channels * size
     out = torch.empty(shape, dtype=data.dtype, device=data.device)
-    if (type(shape[0]) is int and shape[0] == 0) or (type(channels) is int and channels == 0):
-        return out
-    flat = data.reshape(data.shape[0], channels)
-    lib = _lib.load()
-    initial = params["initial"]
-    with _on_device(data.device):
-        rc = lib.nb200_segment_pool(_ptr(flat), dtype_code(data.dtype), data.shape[0], channels,
-                                    flat.stride(0), flat.stride(1), _ptr(spans), shape[0],
-                                    1 if name == "segment_mean" else 0, int(initial is not None),
-                                    _initial_bits(initial), _ptr(out),
-                                    ctypes.c_void_p(current_stream(data.device)))
-    _lib.check(rc, f"neptune {name}")
+    if not ((type(shape[0]) is int and shape[0] == 0) or (type(channels) is int and channels == 0)):
+        flat = data.reshape(data.shape[0], channels)
+        lib = _lib.load()
+        initial = params["initial"]
+        with _on_device(data.device):
+            rc = lib.nb200_segment_pool(_ptr(flat), dtype_code(data.dtype), data.shape[0], channels,
+                                        flat.stride(0), flat.stride(1), _ptr(bounds), idx, bstride, shape[0],
+                                        1 if name == "segment_mean" else 0, int(initial is not None),
+                                        _initial_bits(initial), _ptr(out), _ptr(status),
+                                        ctypes.c_void_p(current_stream(data.device)))
+        _lib.check(rc, f"neptune {name}")
+    if _sync_checks():
+        check_segment_status(segment_status(data.device))
     return out
 
 

@@ -8,7 +8,9 @@
  * generated kernels under Triton's CPU interpreter and its ATen graphs).
  *
  * Build: make -C oracle   (gcc -O2 -fopenmp -ffp-contract=off: no FMA contraction, no
- * reassociation; float arithmetic is IEEE binary32 with round-to-nearest-even).
+ * reassociation; float arithmetic is IEEE binary32 with round-to-nearest-even). Sums are
+ * accumulated in binary64 so the oracle sits closer to the exact value than any fp32 summation
+ * order; storage-dtype rounding (segments, RMSNorm stages) is reproduced exactly.
  *
  * Functions and the reference code they restate:
  *   oracle_fold        serial repaired fold, template.py:41-54 + emitters.py:436-532
@@ -69,27 +71,9 @@ static float phi(int sk, float v, const oparams* p) {
 
 static int floors(int sk) { return sk == SK_STABLE_L2 || sk == SK_LINEAR_ATTN || sk == SK_SUMSQ_DIV; }
 
-static float term(int sk, float v, float den, const oparams* p) {
-    switch (sk) {
-        case SK_STABLE_L2: { float r = v / den; return r * r; }
-        case SK_LINEAR_ATTN: return v / den;
-        case SK_DECAY_RENORM: return v / (den + (float)p->N);
-        case SK_SUMSQ_DIV: return (v * v) * (1.0f / den);
-    }
-    return 0.0f;
-}
-
-static float factor(int sk, float q, float qn, const oparams* p) {
-    switch (sk) {
-        case SK_STABLE_L2: { float r = q / qn; return r * r; }
-        case SK_LINEAR_ATTN: case SK_SUMSQ_DIV: return q / qn;
-        case SK_DECAY_RENORM: return (q + (float)p->N) / (qn + (float)p->N);
-        case SK_RMSNORM_MAX: return sqrtf(q + (float)p->eps) * (1.0f / sqrtf(qn + (float)p->eps));
-    }
-    return 1.0f;
-}
-
-/* The `{sk}_chunk` helper (emitters.py:459-488) over n contiguous values. */
+/* The `{sk}_chunk` helper (emitters.py:459-488) over n contiguous values. As a checker the oracle
+ * evaluates every term and every sum in binary64 (the reference kernel sums fp32 terms in a tree;
+ * a binary64 sum is closer to the exact value than any fp32 order), then stores the state in fp32. */
 static ostate chunk_state(int sk, const float* v, int64_t n, int64_t ncols_total, const oparams* p) {
     ostate s = {-INFINITY, 0.0f, 0, 0};
     if (n <= 0) return s;
@@ -102,31 +86,49 @@ static ostate chunk_state(int sk, const float* v, int64_t n, int64_t ncols_total
             else if (ph == INFINITY) st |= 2;
             else if (ph != -INFINITY) { seen = 1; if (ph > m) m = ph; }
         }
-        float den = seen ? m : 0.0f, acc = 0.0f;
+        double den = seen ? m : 0.0, acc = 0.0;
         for (int64_t i = 0; i < n; ++i) {
             float ph = phi(sk, v[i], p);
-            if (isfinite(ph)) acc += expf(ph - den);
+            if (isfinite(ph)) acc += exp((double)ph - den);
         }
-        s.m = m; s.acc = acc; s.seen = seen; s.status = st;
+        s.m = m; s.acc = (float)acc; s.seen = seen; s.status = st;
         return s;
     }
     if (sk == SK_RMSNORM_MAX) {
-        float invn = (float)(1.0 / (double)ncols_total), m = 0.0f;
-        for (int64_t i = 0; i < n; ++i) m += (v[i] * v[i]) * invn;
-        float r = 1.0f / sqrtf(m + (float)p->eps), acc = -INFINITY;
-        for (int64_t i = 0; i < n; ++i) { float t = v[i] * r; if (t > acc) acc = t; }
-        s.m = m; s.acc = acc; s.seen = 1;
+        double invn = 1.0 / (double)ncols_total, m = 0.0;
+        for (int64_t i = 0; i < n; ++i) m += ((double)v[i] * v[i]) * invn;
+        double r = 1.0 / sqrt(m + p->eps), acc = -INFINITY;
+        for (int64_t i = 0; i < n; ++i) { double t = v[i] * r; if (t > acc) acc = t; }
+        s.m = (float)m; s.acc = (float)acc; s.seen = 1;
         return s;
     }
     float m = 0.0f;
     for (int64_t i = 0; i < n; ++i) { float a = fabsf(v[i]); if (a > m) m = a; }
-    float den = floors(sk) ? fmaxf(m, 1e-30f) : m, acc = 0.0f;
-    for (int64_t i = 0; i < n; ++i) acc += term(sk, v[i], den, p);
-    s.m = m; s.acc = acc; s.seen = 1;
+    double den = floors(sk) ? fmax(m, 1e-30) : m, acc = 0.0;
+    for (int64_t i = 0; i < n; ++i) {
+        double x = v[i];
+        switch (sk) {
+            case SK_STABLE_L2: acc += (x / den) * (x / den); break;
+            case SK_LINEAR_ATTN: acc += x / den; break;
+            case SK_DECAY_RENORM: acc += x / (den + p->N); break;
+            case SK_SUMSQ_DIV: acc += x * x / den; break;
+        }
+    }
+    s.m = m; s.acc = (float)acc; s.seen = 1;
     return s;
 }
 
-/* `{sk}_merge_state` (emitters.py:500-517): A is the left operand. */
+/* `{sk}_merge_state` (emitters.py:500-517): A is the left operand; repairs in binary64. */
+static double factor_d(int sk, double q, double qn, const oparams* p) {
+    switch (sk) {
+        case SK_STABLE_L2: return (q / qn) * (q / qn);
+        case SK_LINEAR_ATTN: case SK_SUMSQ_DIV: return q / qn;
+        case SK_DECAY_RENORM: return (q + p->N) / (qn + p->N);
+        case SK_RMSNORM_MAX: return sqrt(q + p->eps) / sqrt(qn + p->eps);
+    }
+    return 1.0;
+}
+
 static ostate merge_state(int sk, ostate A, ostate B, const oparams* p) {
     ostate r;
     r.status = A.status | B.status;
@@ -135,16 +137,17 @@ static ostate merge_state(int sk, ostate A, ostate B, const oparams* p) {
     r.seen = 1;
     if (is_log(sk)) {
         r.m = fmaxf(A.m, B.m);
-        r.acc = A.acc * expf(A.m - r.m) + B.acc * expf(B.m - r.m);
+        r.acc = (float)((double)A.acc * exp((double)A.m - r.m) + (double)B.acc * exp((double)B.m - r.m));
     } else if (sk == SK_RMSNORM_MAX) {
-        r.m = A.m + B.m;
-        r.acc = fmaxf(A.acc * factor(sk, A.m, r.m, p), B.acc * factor(sk, B.m, r.m, p));
+        double m = (double)A.m + (double)B.m;
+        r.m = (float)m;
+        r.acc = (float)fmax(A.acc * factor_d(sk, A.m, m, p), B.acc * factor_d(sk, B.m, m, p));
     } else {
         int f = floors(sk);
         r.m = fmaxf(A.m, B.m);
-        float qa = f ? fmaxf(A.m, 1e-30f) : A.m, qb = f ? fmaxf(B.m, 1e-30f) : B.m;
-        float qn = f ? fmaxf(r.m, 1e-30f) : r.m;
-        r.acc = A.acc * factor(sk, qa, qn, p) + B.acc * factor(sk, qb, qn, p);
+        double qa = f ? fmax(A.m, 1e-30) : A.m, qb = f ? fmax(B.m, 1e-30) : B.m;
+        double qn = f ? fmax(r.m, 1e-30) : r.m;
+        r.acc = (float)(A.acc * factor_d(sk, qa, qn, p) + B.acc * factor_d(sk, qb, qn, p));
     }
     return r;
 }
@@ -155,22 +158,23 @@ static float finalize(int sk, ostate s, const oparams* p) {
         if (s.status & 1) return NAN;
         if (s.status & 2) return INFINITY;
         if (!s.seen) return -INFINITY;
-        return s.m + logf(s.acc + (float)p->tiny);
+        return (float)((double)s.m + log((double)s.acc + p->tiny));
     }
-    if (sk == SK_STABLE_L2) return fmaxf(s.m, 1e-30f) * sqrtf(s.acc);
+    if (sk == SK_STABLE_L2) return (float)(fmax(s.m, 1e-30) * sqrt((double)s.acc));
     return s.acc;
 }
 
 /* ------------------------------------------------------------------ a1 serial fold */
 void oracle_two_pass(int sk, const float* x, int64_t rows, int64_t ncols, float* out) {
-    const float invn = (float)(1.0 / (double)ncols);
 #pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < rows; ++r) {
         const float* v = x + r * ncols;
-        float m = 0.0f, acc = 0.0f;
-        for (int64_t i = 0; i < ncols; ++i) m += v[i] * invn;
-        for (int64_t i = 0; i < ncols; ++i) { float d = v[i] - m; acc += invn * (d * d); }
-        out[r] = sk == SK_STD ? sqrtf(acc) : acc;
+        double m = 0.0, acc = 0.0;
+        for (int64_t i = 0; i < ncols; ++i) m += v[i];
+        m /= (double)ncols;
+        for (int64_t i = 0; i < ncols; ++i) { double d = v[i] - m; acc += d * d; }
+        acc /= (double)ncols;
+        out[r] = (float)(sk == SK_STD ? sqrt(acc) : acc);
     }
 }
 
@@ -225,9 +229,12 @@ void oracle_softmax(int mode, const float* x, int64_t rows, int64_t ncols, float
         const float* v = x + r * ncols;
         ostate s = chunk_state(SK_LOGSUMEXP, v, ncols, ncols, &p);
         int bad = s.status != 0 || !s.seen;
-        float lg = logf(s.acc);
+        double acc = 0.0;  /* the row's sum again in binary64, unrounded */
+        if (!bad)
+            for (int64_t i = 0; i < ncols; ++i) acc += exp((double)v[i] - s.m);
+        double lg = log(acc);
         for (int64_t i = 0; i < ncols; ++i)
-            y[r * ncols + i] = bad ? NAN : (mode == 0 ? expf(v[i] - s.m) / s.acc : (v[i] - s.m) - lg);
+            y[r * ncols + i] = bad ? NAN : (float)(mode == 0 ? exp((double)v[i] - s.m) / acc : ((double)v[i] - s.m) - lg);
         if (lse) lse[r] = finalize(SK_LOGSUMEXP, s, &p);
     }
 }
@@ -238,7 +245,7 @@ void oracle_l2_normalize(const float* x, int64_t rows, int64_t ncols, int dtype,
     for (int64_t r = 0; r < rows; ++r) {
         const float* v = x + r * ncols;
         float n = finalize(SK_STABLE_L2, chunk_state(SK_STABLE_L2, v, ncols, ncols, &p), &p);
-        for (int64_t i = 0; i < ncols; ++i) y[r * ncols + i] = round_dtype(v[i] / n, dtype);
+        for (int64_t i = 0; i < ncols; ++i) y[r * ncols + i] = round_dtype((float)((double)v[i] / n), dtype);
         if (norm) norm[r] = round_dtype(n, dtype);
     }
 }
@@ -256,8 +263,9 @@ void oracle_rms_norm(const float* x, const float* gamma, int64_t rows, int64_t n
 #pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < rows; ++r) {
         const float* v = x + r * ncols;
-        float total = 0.0f;
-        for (int64_t i = 0; i < ncols; ++i) total += v[i] * v[i];
+        double total_d = 0.0;
+        for (int64_t i = 0; i < ncols; ++i) total_d += (double)v[i] * v[i];
+        float total = (float)total_d;  /* the fp32 total (order-free: binary64 sum, rounded once) */
         float mean = total / count;
         float scale = rsqrt_rn(mean + e);
         for (int64_t i = 0; i < ncols; ++i) {

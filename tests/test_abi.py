@@ -71,8 +71,10 @@ def test_argument_validation_happens_before_any_launch():
     assert lib.nb200_fold(0, ctypes.byref(p), null, 0, 1, 8, 8, 1, null, ctypes.byref(bad_launch), null) \
         == L.NB200_ERR_ARG
     # segments: index dtype and reduce mode
-    assert lib.nb200_segment_spans(null, 5, 1, 1, 0, 0, 1, null, null, null) == L.NB200_ERR_ARG
-    assert lib.nb200_segment_pool(null, 0, 1, 1, 1, 1, null, 1, 7, 0, 0, null, null) == L.NB200_ERR_ARG
+    assert lib.nb200_segment_spans(null, 5, 1, 1, 0, 1, null, null, null) == L.NB200_ERR_ARG
+    assert lib.nb200_segment_pool(null, 0, 1, 1, 1, 1, null, 1, 1, 1, 7, 0, 0, null, null, null) == L.NB200_ERR_ARG
+    assert lib.nb200_segment_pool(null, 0, 1, 1, 1, 1, null, 9, 1, 1, 0, 0, 0, null, null, null) == L.NB200_ERR_ARG
+    assert lib.nb200_segment_pool(null, 0, 1, 4, 4, 1, null, 1, 1, 0, 0, 0, 0, null, null, null) == L.NB200_OK
 
 
 def test_check_maps_status_to_reference_exceptions():

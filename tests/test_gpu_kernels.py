@@ -76,7 +76,7 @@ def test_serial_fold_matches_oracle_all_layouts_and_dtypes(name, oracle_mod):
             assert_close_dtype(got, ref, dtype, atol32=1e-6 * (1 + _scale(ref)))
 
 
-@pytest.mark.parametrize("cfg", [(16384, 1), (16384, 4), (16384, 8), (4096, 16)])
+@pytest.mark.parametrize("cfg", [(16384, 0), (16384, 1), (16384, 4), (16384, 8), (4096, 16)])
 def test_every_launch_variant_agrees(cfg, oracle_mod):
     import torch
 
@@ -314,6 +314,7 @@ def test_segment_spans_status_and_nan_for_invalid_descriptors(monkeypatch):
     import neptune_opt_b200 as NB
     from neptune_opt_b200 import torch_op
 
+    NB.segment_status()  # start from a clear word
     sp = golden("spans.npz")
     labels = sorted({k.rsplit("|", 1)[0] for k in sp.files})
     for label in labels:
@@ -323,8 +324,7 @@ def test_segment_spans_status_and_nan_for_invalid_descriptors(monkeypatch):
         if is_off and segs.numel() == 0:
             continue
         out = NB.run_segment_pool(data, segs, offsets=bool(is_off), unsafe=bool(unsafe))
-        torch.cuda.synchronize()
-        status = int(torch_op.LAST_SEGMENT_STATUS.item())
+        status = NB.segment_status()
         error = str(sp[label + "|error"])
         if not error:
             assert status == 0, label
@@ -336,12 +336,15 @@ def test_segment_spans_status_and_nan_for_invalid_descriptors(monkeypatch):
     monkeypatch.setenv("NEPTUNE_B200_SYNC_CHECKS", "1")
     with pytest.raises(RuntimeError, match="monotonic"):
         NB.run_segment_pool(torch.zeros(7, 2, device="cuda"), torch.tensor([0, 5, 3, 7], device="cuda"), offsets=True)
-    # malformed spans pool to NaN without reading data
+    assert NB.segment_status() == 0  # the failing check cleared the word
+    # malformed spans pool to NaN without reading data; valid neighbours are unaffected
     monkeypatch.setenv("NEPTUNE_B200_SYNC_CHECKS", "0")
-    out = NB.run_segment_pool(torch.ones(7, 2, device="cuda"), torch.tensor([0, 5, 3, 7], device="cuda"),
-                              offsets=True, reduce="sum")
-    got = out.cpu().numpy()
-    assert np.isnan(got[1]).all() and got[0].tolist() == [5.0, 5.0] and got[2].tolist() == [4.0, 4.0]
+    for dtype in DTYPES:
+        out = NB.run_segment_pool(torch.ones(7, 8, device="cuda", dtype=_t(dtype)),
+                                  torch.tensor([0, 5, 3, 7], device="cuda"), offsets=True, reduce="sum")
+        got = out.float().cpu().numpy()
+        assert np.isnan(got[1]).all() and (got[0] == 5.0).all() and (got[2] == 4.0).all()
+    assert NB.segment_status() == 8
 
 
 def test_custom_ops_run_on_gpu_and_match_run():
@@ -373,3 +376,13 @@ def test_launches_are_counted_by_the_library():
     NB.run("logsumexp", torch.randn(4, 100, device="cuda"))
     NB.run_rms_norm(torch.randn(4, 100, device="cuda"), torch.randn(100, device="cuda"))
     assert NB.launch_count() - before == 2
+
+
+def test_streaming_kernels_never_timed_out():
+    """Every bounded wait of the bulk-copy kernels completed in this process."""
+    import torch
+
+    import neptune_opt_b200._lib as L
+
+    torch.cuda.synchronize()
+    assert L.stream_fault() == 0

@@ -174,10 +174,10 @@ def test_segment_status_messages_follow_reference_order():
 
 
 def test_launch_policy_defaults_and_table():
-    assert autotune.best_config(8192, 2048, torch.float32) == (16384, 1)
-    assert autotune.best_config(16384, 4096, torch.bfloat16) == (16384, 1)
-    assert autotune.best_config(512, 262144, torch.bfloat16) == (16384, 8)
-    assert autotune.best_config(4, 100, torch.float32, device="cpu") == (16384, 1)
+    assert autotune.best_config(8192, 2048, torch.float32) == (16384, 0)
+    assert autotune.best_config(16384, 4096, torch.bfloat16) == (16384, 0)
+    assert autotune.best_config(4, 100, torch.float32, device="cpu") == (16384, 0)
+    assert autotune.launch_for((16384, 0)) is None
     assert autotune.machine_key("NVIDIA B200") == "b200"
     assert autotune.shape_key(1, 262144) == ("single", 262144)
     assert autotune.launch_for((16384, 1)).variant == 1
@@ -185,10 +185,10 @@ def test_launch_policy_defaults_and_table():
     for entry in autotune.tables().values():
         for cfg in entry["table"].values():
             assert cfg in autotune.CANDIDATES
-    res = [autotune.Result(16384, 1, 1.0), autotune.Result(16384, 8, 0.97)]
-    assert autotune.choose(res, (16384, 1))[0] == (16384, 1)
-    res = [autotune.Result(16384, 1, 1.0), autotune.Result(16384, 8, 0.5)]
-    assert autotune.choose(res, (16384, 1))[0] == (16384, 8)
+    res = [autotune.Result(16384, 0, 1.0), autotune.Result(16384, 8, 0.97)]
+    assert autotune.choose(res, (16384, 0))[0] == (16384, 0)
+    res = [autotune.Result(16384, 0, 1.0), autotune.Result(16384, 8, 0.5)]
+    assert autotune.choose(res, (16384, 0))[0] == (16384, 8)
 
 
 def test_template_helpers():
