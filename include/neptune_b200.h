@@ -79,9 +79,10 @@ typedef enum {
 
 typedef struct {
     int32_t variant;        /* nb200_variant                                          */
-    int32_t threads;        /* CTA size for NB200_VARIANT_CTA_ROW (64..512, x32)      */
+    int32_t threads;        /* CTA size (64..512, x32); for NB200_VARIANT_STREAM the   */
+                            /* number of warps, each owning its own ring of stages    */
     int32_t ctas_per_sm;    /* persistent grid = SMs * ctas_per_sm (0: default)       */
-    int32_t reserved;
+    int32_t stages;         /* NB200_VARIANT_STREAM: stages per warp ring (0: fit)    */
 } nb200_launch;
 
 /* One partial state of the repaired fold (emitters.py:436-519): raw producer value,
@@ -139,7 +140,8 @@ int64_t nb200_fold_split_scratch_bytes(int64_t rows, int64_t nparts);
 int nb200_fold_split(int skeleton, const nb200_params* params,
                      const void* x, int dtype, int64_t rows, int64_t ncols,
                      int64_t stride_row, int64_t stride_col, int64_t chunk_cols,
-                     void* scratch, int64_t scratch_bytes, void* out, void* stream);
+                     void* scratch, int64_t scratch_bytes, void* out,
+                     const nb200_launch* launch, void* stream);
 
 /* The two halves of the split plan, for callers that move states between devices.
  * nb200_fold_partial folds columns [col_begin, col_begin + ncols_shard) of every row in
@@ -152,7 +154,7 @@ int nb200_fold_partial(int skeleton, const nb200_params* params,
                        const void* x, int dtype, int64_t rows, int64_t ncols_total,
                        int64_t col_begin, int64_t ncols_shard,
                        int64_t stride_row, int64_t stride_col, int64_t chunk_cols,
-                       nb200_state* states, void* stream);
+                       nb200_state* states, const nb200_launch* launch, void* stream);
 int nb200_fold_merge(int skeleton, const nb200_params* params,
                      const nb200_state* states, int64_t rows, int64_t nparts,
                      int64_t row_stride, int64_t part_stride,

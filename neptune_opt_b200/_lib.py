@@ -33,7 +33,7 @@ class NB200Params(ctypes.Structure):
 
 class NB200Launch(ctypes.Structure):
     _fields_ = [("variant", ctypes.c_int32), ("threads", ctypes.c_int32),
-                ("ctas_per_sm", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+                ("ctas_per_sm", ctypes.c_int32), ("stages", ctypes.c_int32)]
 
 
 class NB200State(ctypes.Structure):
@@ -56,9 +56,9 @@ SIGNATURES = {
     "nb200_l2_normalize": (_int, [_vp, _int, _i64, _i64, _i64, _i64, _vp, _vp, ctypes.POINTER(NB200Launch), _vp]),
     "nb200_fold_split_scratch_bytes": (_i64, [_i64, _i64]),
     "nb200_fold_split": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _int, _i64, _i64, _i64, _i64, _i64,
-                                _vp, _i64, _vp, _vp]),
+                                _vp, _i64, _vp, ctypes.POINTER(NB200Launch), _vp]),
     "nb200_fold_partial": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _int, _i64, _i64, _i64, _i64, _i64,
-                                  _i64, _i64, _vp, _vp]),
+                                  _i64, _i64, _vp, ctypes.POINTER(NB200Launch), _vp]),
     "nb200_fold_merge": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
     "nb200_rms_norm": (_int, [_vp, _vp, _int, _i64, _i64, _i64, _i64, _i64, _dbl, _vp,
                               ctypes.POINTER(NB200Launch), _vp]),
@@ -136,5 +136,5 @@ def params_struct(values: dict | None) -> NB200Params:
                        float(v.get("beta", 1.0)), float(v.get("N", 1.0)), float(v.get("eps", 1.0)))
 
 
-def launch_struct(variant: int = VARIANT_AUTO, threads: int = 0, ctas_per_sm: int = 0) -> NB200Launch:
-    return NB200Launch(int(variant), int(threads), int(ctas_per_sm), 0)
+def launch_struct(variant: int = VARIANT_AUTO, threads: int = 0, ctas_per_sm: int = 0, stages: int = 0) -> NB200Launch:
+    return NB200Launch(int(variant), int(threads), int(ctas_per_sm), int(stages))

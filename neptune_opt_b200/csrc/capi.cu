@@ -108,6 +108,7 @@ int check_launch(const nb200_launch* L) {
         set_error("launch threads must be a multiple of 32 in [64, 512]"); return NB200_ERR_ARG;
     }
     if (L->ctas_per_sm < 0 || L->ctas_per_sm > 32) { set_error("ctas_per_sm must be in [0, 32]"); return NB200_ERR_ARG; }
+    if (L->stages < 0 || L->stages > 8) { set_error("stages must be in [0, 8]"); return NB200_ERR_ARG; }
     return NB200_OK;
 }
 
@@ -167,7 +168,8 @@ int64_t nb200_fold_split_scratch_bytes(int64_t rows, int64_t nparts) {
 
 int nb200_fold_partial(int skeleton, const nb200_params* params, const void* x, int dtype, int64_t rows,
                        int64_t ncols_total, int64_t col_begin, int64_t ncols_shard, int64_t stride_row,
-                       int64_t stride_col, int64_t chunk_cols, nb200_state* states, void* stream) {
+                       int64_t stride_col, int64_t chunk_cols, nb200_state* states, const nb200_launch* launch,
+                       void* stream) {
     nb200_params q;
     int rc = check_params(skeleton, params, &q);
     if (rc) return rc;
@@ -178,11 +180,12 @@ int nb200_fold_partial(int skeleton, const nb200_params* params, const void* x, 
         return NB200_ERR_ARG;
     }
     if (chunk_cols <= 0) { set_error("nb200_fold_partial: chunk_cols must be positive"); return NB200_ERR_ARG; }
+    if ((rc = check_launch(launch))) return rc;
     if (rows > 0 && !aligned16(states)) { set_error("nb200_fold_partial: states must be 16-byte aligned"); return NB200_ERR_ARG; }
     if (rows == 0) return NB200_OK;
     const int64_t nparts = (ncols_shard + chunk_cols - 1) / chunk_cols;
     return launch_partial(skeleton, make_params(q, ncols_total), x, dtype, rows, col_begin, ncols_shard,
-                          stride_row, stride_col, chunk_cols, nparts, states, (cudaStream_t)stream);
+                          stride_row, stride_col, chunk_cols, nparts, states, launch, (cudaStream_t)stream);
 }
 
 int nb200_fold_merge(int skeleton, const nb200_params* params, const nb200_state* states, int64_t rows,
@@ -201,7 +204,7 @@ int nb200_fold_merge(int skeleton, const nb200_params* params, const nb200_state
 
 int nb200_fold_split(int skeleton, const nb200_params* params, const void* x, int dtype, int64_t rows,
                      int64_t ncols, int64_t stride_row, int64_t stride_col, int64_t chunk_cols,
-                     void* scratch, int64_t scratch_bytes, void* out, void* stream) {
+                     void* scratch, int64_t scratch_bytes, void* out, const nb200_launch* launch, void* stream) {
     nb200_params q;
     int rc = check_params(skeleton, params, &q);
     if (rc) return rc;
@@ -211,6 +214,7 @@ int nb200_fold_split(int skeleton, const nb200_params* params, const void* x, in
         return NB200_ERR_UNSUPPORTED;
     }
     if (chunk_cols <= 0) { set_error("nb200_fold_split: chunk_cols must be positive"); return NB200_ERR_ARG; }
+    if ((rc = check_launch(launch))) return rc;
     const int64_t nparts = (ncols + chunk_cols - 1) / chunk_cols;
     if (nparts > 4096) {
         set_error("split needs %lld partials, exceeding capacity 4096; use serial", (long long)nparts);
@@ -226,7 +230,7 @@ int nb200_fold_split(int skeleton, const nb200_params* params, const void* x, in
     nb200_state* states = (nb200_state*)scratch;
     const Params p = make_params(q, ncols);
     rc = launch_partial(skeleton, p, x, dtype, rows, 0, ncols, stride_row, stride_col, chunk_cols, nparts,
-                        states, (cudaStream_t)stream);
+                        states, launch, (cudaStream_t)stream);
     if (rc) return rc;
     return launch_merge(skeleton, p, states, rows, nparts, nparts, 1, out, dtype, (cudaStream_t)stream);
 }

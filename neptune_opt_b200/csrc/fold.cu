@@ -428,11 +428,11 @@ int merge_dispatch(int sk, const nb200_state* states, T* out, int64_t rows, int6
 int launch_fold(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t ncols,
                 int64_t srow, int64_t scol, void* out, const nb200_launch* L, cudaStream_t st) {
     if (!L || L->variant == NB200_VARIANT_AUTO || L->variant == NB200_VARIANT_STREAM) {
-        int rc = stream_fold(sk, p, x, dtype, rows, ncols, srow, scol, out, st);
+        int rc = stream_fold(sk, p, x, dtype, rows, ncols, srow, scol, out, L, st);
         // rows too wide for a stage: one warp streams each row, when there are enough rows to
         // occupy every warp slot; otherwise the CTA-per-row register kernel spreads a row wider
         if (rc == 0 && rows >= (int64_t)sm_count() * 8)
-            rc = stream_span(sk, p, x, dtype, rows, 0, ncols, srow, scol, ncols, 1, nullptr, out, 1, st);
+            rc = stream_span(sk, p, x, dtype, rows, 0, ncols, srow, scol, ncols, 1, nullptr, out, 1, L, st);
         if (rc != 0) return rc < 0 ? rc : NB200_OK;
         if (L && L->variant == NB200_VARIANT_STREAM) {
             set_error("nb200_fold: the streaming variant needs contiguous 16-byte-aligned rows");
@@ -445,7 +445,7 @@ int launch_fold(int sk, const Params& p, const void* x, int dtype, int64_t rows,
 int launch_softmax(int mode, const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow,
                    int64_t scol, void* y, void* lse, const nb200_launch* L, cudaStream_t st) {
     if (!L || L->variant == NB200_VARIANT_AUTO || L->variant == NB200_VARIANT_STREAM) {
-        const int rc = stream_softmax(mode, x, dtype, rows, ncols, srow, scol, y, lse, st);
+        const int rc = stream_softmax(mode, x, dtype, rows, ncols, srow, scol, y, lse, L, st);
         if (rc != 0) return rc < 0 ? rc : NB200_OK;
         if (L && L->variant == NB200_VARIANT_STREAM) {
             set_error("nb200_softmax: the streaming variant needs contiguous 16-byte-aligned rows of <= 32 KB");
@@ -458,7 +458,7 @@ int launch_softmax(int mode, const void* x, int dtype, int64_t rows, int64_t nco
 int launch_l2(const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
               void* y, void* norm, const nb200_launch* L, cudaStream_t st) {
     if (!L || L->variant == NB200_VARIANT_AUTO || L->variant == NB200_VARIANT_STREAM) {
-        const int rc = stream_l2(x, dtype, rows, ncols, srow, scol, y, norm, st);
+        const int rc = stream_l2(x, dtype, rows, ncols, srow, scol, y, norm, L, st);
         if (rc != 0) return rc < 0 ? rc : NB200_OK;
         if (L && L->variant == NB200_VARIANT_STREAM) {
             set_error("nb200_l2_normalize: the streaming variant needs contiguous 16-byte-aligned rows of <= 32 KB");
@@ -470,8 +470,8 @@ int launch_l2(const void* x, int dtype, int64_t rows, int64_t ncols, int64_t sro
 
 int launch_partial(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t cb,
                    int64_t ns, int64_t srow, int64_t scol, int64_t cc, int64_t nparts,
-                   nb200_state* states, cudaStream_t st) {
-    const int rc = stream_span(sk, p, x, dtype, rows, cb, ns, srow, scol, cc, nparts, states, nullptr, 0, st);
+                   nb200_state* states, const nb200_launch* L, cudaStream_t st) {
+    const int rc = stream_span(sk, p, x, dtype, rows, cb, ns, srow, scol, cc, nparts, states, nullptr, 0, L, st);
     if (rc != 0) return rc < 0 ? rc : NB200_OK;
     NB200_DTYPE_CASES(dtype, partial_dispatch<T>(sk, (const T*)x, states, rows, cb, ns, srow, scol, cc, nparts, p, st))
 }

@@ -20,7 +20,7 @@ int launch_l2(const void* x, int dtype, int64_t rows, int64_t ncols, int64_t sro
               void* y, void* norm, const nb200_launch* L, cudaStream_t st);
 int launch_partial(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t cb,
                    int64_t ns, int64_t srow, int64_t scol, int64_t cc, int64_t nparts,
-                   nb200_state* states, cudaStream_t st);
+                   nb200_state* states, const nb200_launch* L, cudaStream_t st);
 int launch_merge(int sk, const Params& p, const nb200_state* states, int64_t rows, int64_t nparts,
                  int64_t rs, int64_t ps, void* out, int dtype, cudaStream_t st);
 
@@ -37,16 +37,16 @@ int launch_segment_pool(const void* data, int dtype, int64_t nrows, int64_t chan
 // Streaming (bulk-copy staged) paths: return 1 when launched, 0 when the input is not eligible
 // (the caller then uses the register-tiled kernels), negative on error.
 int stream_fold(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow,
-                int64_t scol, void* out, cudaStream_t st);
+                int64_t scol, void* out, const nb200_launch* L, cudaStream_t st);
 int stream_softmax(int mode, const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
-                   void* y, void* lse, cudaStream_t st);
+                   void* y, void* lse, const nb200_launch* L, cudaStream_t st);
 int stream_l2(const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol, void* y, void* norm,
-              cudaStream_t st);
+              const nb200_launch* L, cudaStream_t st);
 int stream_rms(const void* x, const void* gamma, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
-               int64_t sg, float eps, void* y, cudaStream_t st);
+               int64_t sg, float eps, void* y, const nb200_launch* L, cudaStream_t st);
 int stream_span(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t cb, int64_t ns,
                 int64_t srow, int64_t scol, int64_t cc, int64_t nparts, nb200_state* states, void* out,
-                int finalize, cudaStream_t st);
+                int finalize, const nb200_launch* L, cudaStream_t st);
 int stream_fault_take(unsigned int* bits);
 
 int launch_attention(const void* q, const void* k, const void* v, void* o, float* lse,

@@ -120,7 +120,7 @@ int launch_rms(const void* x, const void* gamma, int dtype, int64_t rows, int64_
                int64_t srow, int64_t scol, int64_t sg, float eps, void* out,
                const nb200_launch* L, cudaStream_t st) {
     if (!L || L->variant == NB200_VARIANT_AUTO || L->variant == NB200_VARIANT_STREAM) {
-        const int rc = stream_rms(x, gamma, dtype, rows, ncols, srow, scol, sg, eps, out, st);
+        const int rc = stream_rms(x, gamma, dtype, rows, ncols, srow, scol, sg, eps, out, L, st);
         if (rc != 0) return rc < 0 ? rc : NB200_OK;
         if (L && L->variant == NB200_VARIANT_STREAM) {
             set_error("nb200_rms_norm: the streaming variant needs contiguous 16-byte-aligned rows of <= 32 KB");

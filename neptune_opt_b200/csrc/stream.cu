@@ -23,7 +23,7 @@ struct RowPlan {
     int64_t rows, ncols, srow;  // srow in elements
     int64_t nblocks;            // ceil(rows / R)
     uint32_t row_bytes, stage_bytes, extra_bytes, bar_offset, stage_offset;
-    int R, S, packed;
+    int R, S, packed, warps;
 };
 
 // ------------------------------------------------------------------ packed arithmetic helpers
@@ -112,8 +112,7 @@ struct FoldOp {
             }
             res = Sk<S>::fin(warp_sum(combine_sum<V>(av)));
         } else {
-            const St s = warp_merge<S>(lane_state<S, T>(v, nv, lane, p), lane, p);
-            res = finalize<S>(s, p);
+            res = finalize<S>(row_state<S, T>(v, nv, lane, p), p);
         }
         if (lane == 0) out[r] = Elem<T>::from_f(res);
     }
@@ -129,7 +128,7 @@ struct SoftmaxOp {
     __device__ __forceinline__ void row(const uint4* v, int64_t r, int lane, const unsigned char*) const {
         constexpr int V = Elem<T>::V;
         const Params p{0.f, 0.f, 1.f, 1.f, 0.f, 0.f, 0.f};
-        const St s = warp_merge<NB200_LOGSUMEXP>(lane_state<NB200_LOGSUMEXP, T>(v, nv, lane, p), lane, p);
+        const St s = row_state<NB200_LOGSUMEXP, T>(v, nv, lane, p);
         const bool bad = s.status != 0 || !s.seen;
         const float m = s.m, inv = 1.0f / s.acc, lg = logf(s.acc);
         T* yrow = y + r * ncols;
@@ -157,8 +156,7 @@ struct L2Op {
     __device__ __forceinline__ void row(const uint4* v, int64_t r, int lane, const unsigned char*) const {
         constexpr int V = Elem<T>::V;
         const Params p{0.f, 0.f, 1.f, 1.f, 0.f, 0.f, 0.f};
-        const St s = warp_merge<NB200_STABLE_L2>(lane_state<NB200_STABLE_L2, T>(v, nv, lane, p), lane, p);
-        const float nrm = finalize<NB200_STABLE_L2>(s, p);
+        const float nrm = finalize<NB200_STABLE_L2>(row_state<NB200_STABLE_L2, T>(v, nv, lane, p), p);
         const float inv = 1.0f / nrm;
         T* yrow = y + r * ncols;
         for (int j = lane; j < nv; j += 32) {
@@ -244,7 +242,7 @@ struct RmsOp {
 
 // ------------------------------------------------------------------ resident-row kernel
 template <typename T, class Op>
-__global__ void __launch_bounds__(256) rows_kernel(const T* __restrict__ x, RowPlan pl, Op op) {
+__global__ void __launch_bounds__(512) rows_kernel(const T* __restrict__ x, RowPlan pl, Op op) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + pl.bar_offset) + warp * pl.S;
@@ -307,7 +305,7 @@ struct SpanPlan {
 };
 
 template <int S_, typename T>
-__global__ void __launch_bounds__(256) span_kernel(const T* __restrict__ x, SpanPlan pl, Params p,
+__global__ void __launch_bounds__(512) span_kernel(const T* __restrict__ x, SpanPlan pl, Params p,
                                                    nb200_state* __restrict__ states, T* __restrict__ out) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int V = Elem<T>::V;
@@ -409,7 +407,10 @@ __global__ void __launch_bounds__(256) span_kernel(const T* __restrict__ x, Span
 // ================================================================== host side
 namespace {
 
-constexpr int kStreamThreads = 256;
+constexpr int kStreamThreads = 128;  // 4 warps per CTA, several CTAs per SM
+constexpr int kSpanWarps = 4;
+constexpr int kSpanStages = 2;
+constexpr uint32_t kSpanStageBytes = 4096;  // small sub-blocks: more CTAs (warps) per SM
 constexpr uint32_t kSmemBudget = 224 * 1024;
 
 inline uint32_t align_up(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
@@ -434,7 +435,8 @@ bool rows_streamable(const T* x, int64_t rows, int64_t ncols, int64_t srow, int6
            rb <= 32768;
 }
 
-bool make_row_plan(int64_t rows, int64_t ncols, int64_t srow, size_t esize, uint32_t extra, RowPlan& pl) {
+bool make_row_plan(int64_t rows, int64_t ncols, int64_t srow, size_t esize, uint32_t extra, RowPlan& pl,
+                   int nw, int want_stages) {
     pl.rows = rows;
     pl.ncols = ncols;
     pl.srow = srow;
@@ -446,26 +448,27 @@ bool make_row_plan(int64_t rows, int64_t ncols, int64_t srow, size_t esize, uint
     pl.stage_bytes = align_up((uint32_t)R * pl.row_bytes, 128);
     pl.nblocks = (rows + R - 1) / R;
     pl.extra_bytes = align_up(extra, 128);
-    const int nw = kStreamThreads / 32;
     pl.bar_offset = pl.extra_bytes;
-    pl.stage_offset = align_up(pl.bar_offset + nw * 4 * 8, 128);
-    int S = (int)((kSmemBudget - pl.stage_offset) / ((uint32_t)nw * pl.stage_bytes));
-    S = std::min(S, 4);
-    if (S < 2) return false;
+    pl.stage_offset = align_up(pl.bar_offset + nw * 8 * 8, 128);
+    const int fit = (int)((kSmemBudget - pl.stage_offset) / ((uint32_t)nw * pl.stage_bytes));
+    const int S = want_stages > 0 ? want_stages : std::min(fit, 2);
+    if (S < 2 || S > fit || S > 8) return false;
     pl.S = S;
+    pl.warps = nw;
     return true;
 }
 
-uint32_t row_smem(const RowPlan& pl) { return pl.stage_offset + (uint32_t)(kStreamThreads / 32) * pl.S * pl.stage_bytes; }
+uint32_t row_smem(const RowPlan& pl) { return pl.stage_offset + (uint32_t)pl.warps * pl.S * pl.stage_bytes; }
 
 template <typename T, class Op>
-int launch_rows(const T* x, const RowPlan& pl, const Op& op, cudaStream_t st, const char* what) {
+int launch_rows(const T* x, const RowPlan& pl, const Op& op, cudaStream_t st, const char* what, int cps) {
     auto k = rows_kernel<T, Op>;
     const uint32_t smem = row_smem(pl);
     int rc = ensure_smem(k, smem);
     if (rc) return rc;
-    const int g = persistent_grid(k, kStreamThreads, smem, (pl.nblocks + 7) / 8, 0);
-    k<<<g, kStreamThreads, smem, st>>>(x, pl, op);
+    const int threads = pl.warps * 32;
+    const int g = persistent_grid(k, threads, smem, (pl.nblocks + pl.warps - 1) / pl.warps, cps);
+    k<<<g, threads, smem, st>>>(x, pl, op);
     count_launch();
     return finish_launch(what);
 }
@@ -485,16 +488,20 @@ int stream_fault_take(unsigned int* bits) {
 
 // Returns 1 (and launches) when the streaming path applies, 0 when the caller should use the
 // register-tiled kernels, negative on error.
+inline int plan_warps(const nb200_launch* L) { return (L && L->threads) ? L->threads / 32 : kStreamThreads / 32; }
+inline int plan_stages(const nb200_launch* L) { return L ? L->stages : 0; }
+inline int plan_cps(const nb200_launch* L) { return L ? L->ctas_per_sm : 0; }
+
 template <typename T>
 int stream_fold_t(int sk, const Params& p, const T* x, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
-                  T* out, cudaStream_t st) {
+                  T* out, const nb200_launch* L, cudaStream_t st) {
     if (!rows_streamable(x, rows, ncols, srow, scol)) return 0;
     RowPlan pl;
-    if (!make_row_plan(rows, ncols, srow, sizeof(T), 0, pl)) return 0;
+    if (!make_row_plan(rows, ncols, srow, sizeof(T), 0, pl, plan_warps(L), plan_stages(L))) return 0;
     const int nv = (int)(ncols / Elem<T>::V);
     int rc;
     switch (sk) {
-#define X(S) case S: rc = launch_rows(x, pl, FoldOp<S, T>{out, p, nv}, st, "nb200_fold"); break;
+#define X(S) case S: rc = launch_rows(x, pl, FoldOp<S, T>{out, p, nv}, st, "nb200_fold", plan_cps(L)); break;
         X(NB200_LOGSUMEXP) X(NB200_LSE_BIASED) X(NB200_LSE_SCALED) X(NB200_SOFTCAP_LSE) X(NB200_STABLE_L2)
         X(NB200_LINEAR_ATTN) X(NB200_DECAY_RENORM) X(NB200_SUMSQ_DIV) X(NB200_RMSNORM_MAX) X(NB200_VARIANCE)
         X(NB200_STD)
@@ -506,40 +513,45 @@ int stream_fold_t(int sk, const Params& p, const T* x, int64_t rows, int64_t nco
 
 template <typename T>
 int stream_softmax_t(int mode, const T* x, int64_t rows, int64_t ncols, int64_t srow, int64_t scol, T* y, T* lse,
-                     cudaStream_t st) {
+                     const nb200_launch* L, cudaStream_t st) {
     if (!rows_streamable(x, rows, ncols, srow, scol) || !aligned16(y)) return 0;
     RowPlan pl;
-    if (!make_row_plan(rows, ncols, srow, sizeof(T), 0, pl)) return 0;
-    const int rc = launch_rows(x, pl, SoftmaxOp<T>{y, lse, ncols, (int)(ncols / Elem<T>::V), mode}, st, "nb200_softmax");
+    if (!make_row_plan(rows, ncols, srow, sizeof(T), 0, pl, plan_warps(L), plan_stages(L))) return 0;
+    const int rc = launch_rows(x, pl, SoftmaxOp<T>{y, lse, ncols, (int)(ncols / Elem<T>::V), mode}, st, "nb200_softmax",
+                               plan_cps(L));
     return rc ? rc : 1;
 }
 
 template <typename T>
-int stream_l2_t(const T* x, int64_t rows, int64_t ncols, int64_t srow, int64_t scol, T* y, T* norm, cudaStream_t st) {
+int stream_l2_t(const T* x, int64_t rows, int64_t ncols, int64_t srow, int64_t scol, T* y, T* norm,
+                const nb200_launch* L, cudaStream_t st) {
     if (!rows_streamable(x, rows, ncols, srow, scol) || !aligned16(y)) return 0;
     RowPlan pl;
-    if (!make_row_plan(rows, ncols, srow, sizeof(T), 0, pl)) return 0;
-    const int rc = launch_rows(x, pl, L2Op<T>{y, norm, ncols, (int)(ncols / Elem<T>::V)}, st, "nb200_l2_normalize");
+    if (!make_row_plan(rows, ncols, srow, sizeof(T), 0, pl, plan_warps(L), plan_stages(L))) return 0;
+    const int rc = launch_rows(x, pl, L2Op<T>{y, norm, ncols, (int)(ncols / Elem<T>::V)}, st, "nb200_l2_normalize",
+                               plan_cps(L));
     return rc ? rc : 1;
 }
 
 template <typename T>
 int stream_rms_t(const T* x, const T* gamma, int64_t rows, int64_t ncols, int64_t srow, int64_t scol, int64_t sg,
-                 float eps, T* y, cudaStream_t st) {
+                 float eps, T* y, const nb200_launch* L, cudaStream_t st) {
     if (!rows_streamable(x, rows, ncols, srow, scol) || !aligned16(y)) return 0;
     RowPlan pl;
-    if (!make_row_plan(rows, ncols, srow, sizeof(T), (uint32_t)(ncols * (int64_t)sizeof(T)), pl)) return 0;
+    if (!make_row_plan(rows, ncols, srow, sizeof(T), (uint32_t)(ncols * (int64_t)sizeof(T)), pl, plan_warps(L),
+                       plan_stages(L)))
+        return 0;
     const RmsOp<T> op{y, gamma, ncols, sg, (int)(ncols / Elem<T>::V), eps, static_cast<float>(ncols)};
-    const int rc = launch_rows(x, pl, op, st, "nb200_rms_norm");
+    const int rc = launch_rows(x, pl, op, st, "nb200_rms_norm", plan_cps(L));
     return rc ? rc : 1;
 }
 
-// Column spans [cb + part * cc, ...) of every row, staged through 8 KB sub-blocks. finalize = 1
+// Column spans [cb + part * cc, ...) of every row, staged through 4 KB sub-blocks. finalize = 1
 // requires nparts == 1 (a whole row per item) and writes out[rows].
 template <typename T>
 int stream_span_t(int sk, const Params& p, const T* x, int64_t rows, int64_t cb, int64_t ns, int64_t srow,
                   int64_t scol, int64_t cc, int64_t nparts, nb200_state* states, T* out, int finalize,
-                  cudaStream_t st) {
+                  const nb200_launch* L, cudaStream_t st) {
     constexpr int V = Elem<T>::V;
     if (scol != 1 || !aligned16(x) || (rows > 1 && (srow * (int64_t)sizeof(T)) % 16 != 0) || cb % V || ns % V ||
         cc % V)
@@ -553,21 +565,22 @@ int stream_span_t(int sk, const Params& p, const T* x, int64_t rows, int64_t cb,
     pl.cc = cc;
     pl.nparts = nparts;
     pl.nitems = rows * nparts;
-    pl.sub_cols = 8192 / (int64_t)sizeof(T);
+    pl.sub_cols = kSpanStageBytes / (int64_t)sizeof(T);
     pl.nsub = (int)((cc + pl.sub_cols - 1) / pl.sub_cols);
-    pl.stage_bytes = 8192;
+    pl.stage_bytes = kSpanStageBytes;
     pl.bar_offset = 0;
-    const int nw = kStreamThreads / 32;
-    pl.stage_offset = align_up(nw * 4 * 8, 128);
-    pl.S = 3;
+    const int nw = (L && L->threads) ? L->threads / 32 : kSpanWarps;
+    pl.stage_offset = align_up(nw * 8 * 8, 128);
+    pl.S = (L && L->stages) ? L->stages : kSpanStages;
+    if (pl.S < 2 || pl.stage_offset + (uint32_t)nw * pl.S * pl.stage_bytes > kSmemBudget) return 0;
     pl.finalize = finalize;
     const uint32_t smem = pl.stage_offset + (uint32_t)nw * pl.S * pl.stage_bytes;
     int rc = NB200_OK;
     auto go = [&](auto k) {
         rc = ensure_smem(k, smem);
         if (rc) return;
-        const int g = persistent_grid(k, kStreamThreads, smem, (pl.nitems + nw - 1) / nw, 0);
-        k<<<g, kStreamThreads, smem, st>>>(x, pl, p, states, out);
+        const int g = persistent_grid(k, nw * 32, smem, (pl.nitems + nw - 1) / nw, L ? L->ctas_per_sm : 0);
+        k<<<g, nw * 32, smem, st>>>(x, pl, p, states, out);
         count_launch();
         rc = finish_launch(finalize ? "nb200_fold" : "nb200_fold_partial");
     };
@@ -590,26 +603,27 @@ int stream_span_t(int sk, const Params& p, const T* x, int64_t rows, int64_t cb,
     return 0;
 
 int stream_fold(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow,
-                int64_t scol, void* out, cudaStream_t st) {
-    NB200_STREAM_DTYPES(dtype, stream_fold_t<T>(sk, p, (const T*)x, rows, ncols, srow, scol, (T*)out, st))
+                int64_t scol, void* out, const nb200_launch* L, cudaStream_t st) {
+    NB200_STREAM_DTYPES(dtype, stream_fold_t<T>(sk, p, (const T*)x, rows, ncols, srow, scol, (T*)out, L, st))
 }
 int stream_softmax(int mode, const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
-                   void* y, void* lse, cudaStream_t st) {
-    NB200_STREAM_DTYPES(dtype, stream_softmax_t<T>(mode, (const T*)x, rows, ncols, srow, scol, (T*)y, (T*)lse, st))
+                   void* y, void* lse, const nb200_launch* L, cudaStream_t st) {
+    NB200_STREAM_DTYPES(dtype, stream_softmax_t<T>(mode, (const T*)x, rows, ncols, srow, scol, (T*)y, (T*)lse, L, st))
 }
 int stream_l2(const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol, void* y, void* norm,
-              cudaStream_t st) {
-    NB200_STREAM_DTYPES(dtype, stream_l2_t<T>((const T*)x, rows, ncols, srow, scol, (T*)y, (T*)norm, st))
+              const nb200_launch* L, cudaStream_t st) {
+    NB200_STREAM_DTYPES(dtype, stream_l2_t<T>((const T*)x, rows, ncols, srow, scol, (T*)y, (T*)norm, L, st))
 }
 int stream_rms(const void* x, const void* gamma, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
-               int64_t sg, float eps, void* y, cudaStream_t st) {
-    NB200_STREAM_DTYPES(dtype, stream_rms_t<T>((const T*)x, (const T*)gamma, rows, ncols, srow, scol, sg, eps, (T*)y, st))
+               int64_t sg, float eps, void* y, const nb200_launch* L, cudaStream_t st) {
+    NB200_STREAM_DTYPES(dtype, stream_rms_t<T>((const T*)x, (const T*)gamma, rows, ncols, srow, scol, sg, eps, (T*)y, L,
+                                               st))
 }
 int stream_span(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t cb, int64_t ns,
                 int64_t srow, int64_t scol, int64_t cc, int64_t nparts, nb200_state* states, void* out,
-                int finalize, cudaStream_t st) {
+                int finalize, const nb200_launch* L, cudaStream_t st) {
     NB200_STREAM_DTYPES(dtype, stream_span_t<T>(sk, p, (const T*)x, rows, cb, ns, srow, scol, cc, nparts, states,
-                                                (T*)out, finalize, st))
+                                                (T*)out, finalize, L, st))
 }
 
 }  // namespace nb200

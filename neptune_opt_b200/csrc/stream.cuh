@@ -240,4 +240,81 @@ __device__ __forceinline__ St warp_merge(St s, int lane, const Params& p) {
     return s;
 }
 
+// State of a whole resident row, computed the way the reference computes one chunk
+// (emitters.py:459-488): the producer is reduced across the warp first, then every lane forms its
+// terms against the row's producer and the consumer is reduced across the warp. No repair is
+// needed inside a row, so this costs two warp reductions instead of a 32-state merge tree.
+template <int S, typename T>
+__device__ __forceinline__ St row_state(const uint4* v, int nv, int lane, const Params& p) {
+    using K = Sk<S>;
+    constexpr int V = Elem<T>::V;
+    if constexpr (K::kind == K_LOG) {
+        float mv[V], probe[V];
+#pragma unroll
+        for (int e = 0; e < V; ++e) { mv[e] = -NB200_INF; probe[e] = 0.f; }
+        for (int j = lane; j < nv; j += 32) {
+            const uint4 u = v[j];
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+                const float ph = K::phi(Elem<T>::lane(u, e), p);
+                mv[e] = fmaxf(mv[e], ph);
+                probe[e] = fmaf(ph, 0.f, probe[e]);
+            }
+        }
+        const float mall = warp_max(combine_max<V>(mv));
+        const bool finite = __all_sync(0xffffffffu, combine_sum<V>(probe) == 0.f);
+        if (finite) {
+            const bool seen = mall != -NB200_INF;
+            float av[V];
+#pragma unroll
+            for (int e = 0; e < V; ++e) av[e] = 0.f;
+            if (seen) {
+                const float nm = -mall * kLog2e;
+                for (int j = lane; j < nv; j += 32) {
+                    const uint4 u = v[j];
+#pragma unroll
+                    for (int e = 0; e < V; ++e) av[e] += ex2(fmaf(K::phi(Elem<T>::lane(u, e), p), kLog2e, nm));
+                }
+            }
+            return St{mall, warp_sum(combine_sum<V>(av)), seen ? 1 : 0, 0};
+        }
+        // a non-finite element: lane states with exact status, merged (rare path)
+        return warp_merge<S>(lane_state<S, T>(v, nv, lane, p), lane, p);
+    } else if constexpr (K::kind == K_MAXABS) {
+        float mv[V], av[V];
+#pragma unroll
+        for (int e = 0; e < V; ++e) { mv[e] = 0.f; av[e] = 0.f; }
+        for (int j = lane; j < nv; j += 32) {
+            const uint4 u = v[j];
+#pragma unroll
+            for (int e = 0; e < V; ++e) mv[e] = fmaxf(mv[e], fabsf(Elem<T>::lane(u, e)));
+        }
+        const float m = warp_max(combine_max<V>(mv));
+        const float c = K::prep(K::floor ? fmaxf(m, 1e-30f) : m, p);
+        for (int j = lane; j < nv; j += 32) {
+            const uint4 u = v[j];
+#pragma unroll
+            for (int e = 0; e < V; ++e) av[e] += K::term_r(Elem<T>::lane(u, e), c);
+        }
+        return St{m, warp_sum(combine_sum<V>(av)), 1, 0};
+    } else {  // K_SUMMAX
+        float sv[V], av[V];
+#pragma unroll
+        for (int e = 0; e < V; ++e) { sv[e] = 0.f; av[e] = -NB200_INF; }
+        for (int j = lane; j < nv; j += 32) {
+            const uint4 u = v[j];
+#pragma unroll
+            for (int e = 0; e < V; ++e) sv[e] += K::operand(Elem<T>::lane(u, e), p);
+        }
+        const float m = warp_sum(combine_sum<V>(sv));
+        const float r = K::term_scale(m, p);
+        for (int j = lane; j < nv; j += 32) {
+            const uint4 u = v[j];
+#pragma unroll
+            for (int e = 0; e < V; ++e) av[e] = fmaxf(av[e], Elem<T>::lane(u, e) * r);
+        }
+        return St{m, warp_max(combine_max<V>(av)), 1, 0};
+    }
+}
+
 }  // namespace nb200

@@ -98,7 +98,7 @@ def _cuda_partial(name, params, x_shard, col_begin, ncols_total, chunk):
     with _on_device(x_shard.device):
         rc = lib.nb200_fold_partial(SKELETONS[name].id, ctypes.byref(p), ctypes.c_void_p(x_shard.data_ptr()),
                                     dtype_code(x_shard.dtype), rows, ncols_total, 0, width, x_shard.stride(0),
-                                    x_shard.stride(1), chunk, ctypes.c_void_p(states.data_ptr()),
+                                    x_shard.stride(1), chunk, ctypes.c_void_p(states.data_ptr()), None,
                                     ctypes.c_void_p(current_stream(x_shard.device)))
     _lib.check(rc, f"neptune {name} partial")
     return states

@@ -142,7 +142,7 @@ def launch_reduction(name, plan, x2, out, rows, ncols, block=None, num_warps=Non
         scratch = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=x2.device)
         rc = lib.nb200_fold_split(sk.id, ctypes.byref(p), _ptr(x2), dtype_code(x2.dtype), rows, ncols,
                                   x2.stride(0), x2.stride(1), block, _ptr(scratch), scratch.numel(),
-                                  _ptr(out), stream)
+                                  _ptr(out), None, stream)
         _lib.check(rc, f"neptune {name} (split)")
 
 

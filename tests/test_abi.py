@@ -59,10 +59,10 @@ def test_argument_validation_happens_before_any_launch():
     # zero rows is a successful no-op
     assert lib.nb200_fold(0, ctypes.byref(p), null, 0, 0, 8, 8, 1, null, None, null) == L.NB200_OK
     # split capacity and two-pass refusal
-    assert lib.nb200_fold_split(0, ctypes.byref(p), null, 0, 0, 4097, 4097, 1, 1, null, 0, null, null) \
+    assert lib.nb200_fold_split(0, ctypes.byref(p), null, 0, 0, 4097, 4097, 1, 1, null, 0, null, None, null) \
         == L.NB200_ERR_CAPACITY
     assert "capacity" in L.last_error()
-    assert lib.nb200_fold_split(9, ctypes.byref(p), null, 0, 0, 8, 8, 1, 4, null, 0, null, null) \
+    assert lib.nb200_fold_split(9, ctypes.byref(p), null, 0, 0, 8, 8, 1, 4, null, 0, null, None, null) \
         == L.NB200_ERR_UNSUPPORTED
     assert lib.nb200_fold_split_scratch_bytes(3, 5) == 3 * 5 * 16
     # RMSNorm eps and launch policy checks

@@ -178,7 +178,7 @@ def test_partial_and_merge_through_the_c_abi_across_column_shards(oracle_mod):
             nparts = -(-width // chunk)
             st = torch.empty(64 * nparts * 4, dtype=torch.int32, device="cuda")
             rc = lib.nb200_fold_partial(sk, ctypes.byref(p), ctypes.c_void_p(x.data_ptr()), 1, 64, 50000, begin,
-                                        width, x.stride(0), 1, chunk, ctypes.c_void_p(st.data_ptr()), stream)
+                                        width, x.stride(0), 1, chunk, ctypes.c_void_p(st.data_ptr()), None, stream)
             L.check(rc, "partial")
             states.append(st.view(64, nparts, 4))
         allst = torch.cat(states, dim=1).contiguous()
