@@ -298,7 +298,7 @@ def make_segments(torch, NB, seed, reduce="sum"):
         _launch_segment("segment_" + reduce, data, offsets, params, "serial")
 
     return {"name": f"segment_{reduce}", "step": step,
-            "bytes": T * channels * 2 + (nseg + 1) * 8 * 2 + nseg * channels * 2, "rows": nseg, "launches": 2,
+            "bytes": T * channels * 2 + (nseg + 1) * 8 + nseg * channels * 2, "rows": nseg, "launches": 1,
             "buffers": 1, "T": T,
             "desc": f"ordered segment_{reduce} fp16 data[{T},{channels}], {nseg} segments Poisson(20) in [1,200], int64 offsets"}
 
