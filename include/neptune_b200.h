@@ -143,6 +143,20 @@ int nb200_fold_split(int skeleton, const nb200_params* params,
                      void* scratch, int64_t scratch_bytes, void* out,
                      const nb200_launch* launch, void* stream);
 
+/* The split plan for callers that cannot allocate device memory (a host that hands over only its
+ * input and output buffers, a fixed device-memory budget, a path where an allocation would
+ * synchronise). Same arguments and result as nb200_fold_split minus the scratch: the chunk states
+ * live in a 4 MiB array built into the library, which every GPU that loads the library holds until
+ * exit. Limit: rows * ceil(ncols / chunk_cols) <= NB200_NOALLOC_MAX_STATES, else NB200_ERR_CAPACITY.
+ * The first call on a device resolves the array's device address (make it before any stream
+ * capture). Calls share the array: calls that overlap on the GPU race. Allocates nothing.
+ * No counterpart in the reference, whose split plan always allocates its scratch with torch. */
+#define NB200_NOALLOC_MAX_STATES 262144
+int nb200_fold_split_noalloc(int skeleton, const nb200_params* params,
+                             const void* x, int dtype, int64_t rows, int64_t ncols,
+                             int64_t stride_row, int64_t stride_col, int64_t chunk_cols,
+                             void* out, void* stream);
+
 /* The two halves of the split plan, for callers that move states between devices.
  * nb200_fold_partial folds columns [col_begin, col_begin + ncols_shard) of every row in
  * chunk_cols chunks into states[rows * nparts] (nparts = ceil(ncols_shard / chunk_cols)).

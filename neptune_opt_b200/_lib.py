@@ -57,6 +57,8 @@ SIGNATURES = {
     "nb200_fold_split_scratch_bytes": (_i64, [_i64, _i64]),
     "nb200_fold_split": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _int, _i64, _i64, _i64, _i64, _i64,
                                 _vp, _i64, _vp, ctypes.POINTER(NB200Launch), _vp]),
+    "nb200_fold_split_noalloc": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _int, _i64, _i64, _i64, _i64,
+                                        _i64, _vp, _vp]),
     "nb200_fold_partial": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _int, _i64, _i64, _i64, _i64, _i64,
                                   _i64, _i64, _vp, ctypes.POINTER(NB200Launch), _vp]),
     "nb200_fold_merge": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
