@@ -506,6 +506,7 @@ def main():
                 "pct_of_8TBs": round(100 * r["bytes"] / (rms_ * 1e-3) / 1e9 / NOMINAL_HBM_GBS, 2),
                 "roofline_frac_of_measured": round(r["bytes"] / (rms_ * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
                 "algorithmic_bytes_per_step": r["bytes"], "launches_per_step": r["launches"],
+                "traffic_bytes_per_launch": profile_traffic(r["name"]),
                 "l2_rotation_buffers": r["buffers"]}
             del r
             torch.cuda.empty_cache()
