@@ -99,8 +99,9 @@ const char* nb200_last_error(void);
 const char* nb200_version(void);
 /* Number of nb200 kernel launches issued by this process (for launch accounting). */
 uint64_t nb200_launch_count(void);
-/* Reads and clears the fault bits of the streaming kernels (bit 0: a bounded wait on a bulk copy
- * ran out and the kernel stopped early). Synchronous. No counterpart in the reference, whose
+/* Reads and clears the fault bits of the kernels with device-side waits (bit 0: a bounded wait
+ * on a bulk copy in a streaming kernel ran out and the kernel stopped early; bit 1: a bounded wait
+ * in the attention kernel ran out and its output was left unwritten). Synchronous. No counterpart in the reference, whose
  * Triton kernels have no device-side waits. */
 int nb200_stream_fault(uint32_t* bits);
 
@@ -209,9 +210,11 @@ int nb200_segment_pool(const void* data, int dtype, int64_t nrows, int64_t chann
 
 /* ------------------------------------------------------------------ a9: attention
  * O = softmax(scale * Q K^T [+ causal mask]) V per (batch, head), bf16 in/out with
- * fp32 online max/sum repair; lse (nullable) receives fp32 log-sum-exp per query row.
- * Q, K, V, O are contiguous [B, H, S, D]. No counterpart in the reference (its
- * roadmap declares attention out of scope: docs/roadmap.md:28-31). */
+ * fp32 online max/sum repair; lse (nullable) receives fp32 natural log-sum-exp of the scaled
+ * scores per query row, [B, H, S]. Q, K, V, O are contiguous [B, H, S, D], 16-byte aligned;
+ * head_dim must be 128 (else NB200_ERR_UNSUPPORTED) and scale > 0. causal != 0 masks key > query.
+ * No counterpart in the reference (its roadmap declares attention out of scope:
+ * docs/roadmap.md:28-31). */
 int nb200_attention(const void* q, const void* k, const void* v, void* o, float* lse,
                     int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                     int causal, float scale, void* stream);

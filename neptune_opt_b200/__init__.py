@@ -16,6 +16,7 @@ from __future__ import annotations
 
 from neptune_opt_b200 import autotune  # noqa: F401
 from neptune_opt_b200._lib import BackendUnavailable, LIB_PATH, launch_count, load  # noqa: F401
+from neptune_opt_b200.attention import attention_op, run_attention  # noqa: F401
 from neptune_opt_b200.skeletons import (SKELETONS, all_registered, op_parameters, param_defaults,  # noqa: F401
                                         supported)
 from neptune_opt_b200.template import (MAX_SPLIT_PARTS, launch_reduction, run, run_l2_normalize,  # noqa: F401
@@ -66,6 +67,11 @@ def rms_norm(x, gamma, eps: float = 1e-6, plan: str = "serial"):
     return run_rms_norm(x, gamma, eps=eps, plan=plan)
 
 
+def attention(q, k, v, *, causal: bool = False, scale=None, return_lse: bool = False):
+    """softmax(scale * q k^T [+ causal mask]) v over bf16 [batch, heads, seq, 128] tensors."""
+    return run_attention(q, k, v, causal=causal, scale=scale, return_lse=return_lse)
+
+
 def segment_sum(data, segments, *, offsets=False, initial=None, unsafe=False):
     return run_segment_pool(data, segments, reduce="sum", offsets=offsets, initial=initial, unsafe=unsafe)
 
@@ -76,6 +82,7 @@ def segment_mean(data, segments, *, offsets=False, initial=None, unsafe=False):
 
 __all__ = [
     "MAX_SPLIT_PARTS", "SKELETONS", "BackendUnavailable", "all_registered", "as_cuda_op", "as_segment_op",
+    "attention", "attention_op", "run_attention",
     "as_state_op", "as_triton_op", "autotune", "check_segment_status", "cuda_op_name", "l2_normalize",
     "launch_count", "log_softmax", "op_handle", "op_parameters", "param_defaults", "rms_norm", "run",
     "run_l2_normalize", "run_rms_norm", "run_segment_pool", "run_softmax", "run_softmax_lse",

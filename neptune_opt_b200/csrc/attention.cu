@@ -1,15 +1,485 @@
-// Fused attention entry point. The tcgen05/TMEM kernel is built in attention_sm100.cu when
-// present; until then the launcher reports the request as unsupported instead of computing it
-// any other way.
+// Fused single-pass attention forward, O = softmax(scale * Q K^T [+ causal mask]) V, bf16 in and
+// out, fp32 scores and online max/sum repair, on the sm_100a tensor cores.
+//
+// One CTA owns 256 query rows of one (batch, head): two query tiles of 128 rows, one tensor-memory
+// lane per row. The K/V sequence streams through a ring of shared-memory stages filled by
+// tensor-map (TMA) loads; one thread issues the tcgen05 MMAs; two softmax warpgroups, one per
+// query tile, hold one query row per thread.
+//
+//   warp 9      producer: Q tiles once, then K_0, V_0, K_1, V_1, ... into the stage ring
+//   warp 8      MMA: S_t = Q_t K_j^T (shared x shared -> TMEM, fp32)
+//                    O_t += P_t V_j    (P from TMEM, V from shared -> TMEM, fp32)
+//   warps 0-7   softmax for tile t = warp / 4: read S_t, update the running max (log2 domain),
+//               rescale O_t in TMEM when the max grew by more than 2^8, write P_t = 2^(s - m)
+//               as bf16 into the upper half of S_t's columns, accumulate the row sum;
+//               at the end O_t / l -> bf16 -> shared -> TMA store, and the row's log-sum-exp.
+//
+// TMEM (512 columns x 128 lanes of 32 bits): S_0 [0,128), S_1 [128,256), O_0 [256,384),
+// O_1 [384,512); P_t occupies columns [64,128) of S_t.
+//
+// MMA issue order per key tile j: PV_0(j), S_0(j+1), PV_1(j), S_1(j+1). tcgen05.commit arrives
+// only when every earlier MMA of the issuing thread has finished, so the arrival of S_t(j+1)
+// also means PV_t(j) is complete: the softmax warps may rescale O_t between reading S_t(j+1) and
+// publishing P_t(j+1) without a separate barrier. S_t(j+1) overwrites the columns PV_t(j) reads
+// P_t(j) from; the tensor pipe executes one thread's MMAs in issue order.
+//
+// Every wait is bounded (about a second of SM clock). A wait that runs out sets bit 1 of the
+// attention fault word and the CTA's abort flag; the other roles stop at their next wait, the
+// producer waits for the copies it issued, the MMA thread waits for its MMAs, and the CTA frees
+// its tensor memory and exits with the output unwritten.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
 #include "launch.h"
+#include "tcgen05.cuh"
 
 namespace nb200 {
+namespace {
 
-int launch_attention(const void*, const void*, const void*, void*, float*, int64_t, int64_t, int64_t,
-                     int64_t, int, float, cudaStream_t) {
-    set_error("nb200_attention: the tcgen05 attention kernel is not built in this library");
-    return NB200_ERR_UNSUPPORTED;
+static __device__ unsigned int g_attn_fault = 0u;
+
+constexpr int kRows = 128;   // query rows per tile (= TMEM lanes)
+constexpr int kQTiles = 2;   // query tiles per CTA
+constexpr int kKeys = 128;   // keys per K/V tile
+constexpr int kDim = 128;    // head dimension
+constexpr int kStages = 4;   // K/V ring stages; each holds one K or one V tile
+constexpr uint32_t kTileBytes = kRows * kDim * 2;  // 32 KB per Q, K or V tile
+constexpr uint32_t kHalfBytes = kTileBytes / 2;    // one 64-column half: the TMA box
+constexpr int kMmaWarp = 8;
+constexpr int kLoadWarp = 9;
+constexpr int kThreads = 320;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS0 = 0, kColO0 = 256;  // tile t: S at kColS0 + 128 t, O at kColO0 + 128 t
+constexpr uint32_t kColP = 64;                // P inside S's columns
+constexpr float kRescaleSlack = 8.f;          // keep a stale max while the new one is < 2^8 above it
+constexpr uint32_t kIdescQK = tc::idesc_bf16(128, 128, false);
+constexpr uint32_t kIdescPV = tc::idesc_bf16(128, 128, true);
+constexpr long long kWaitCycles = 1ll << 31;
+
+// Shared-memory layout (offsets from a 1024-byte aligned base).
+constexpr uint32_t kOffQ = 0;                                // kQTiles tiles
+constexpr uint32_t kOffKV = kOffQ + kQTiles * kTileBytes;    // kStages tiles
+constexpr uint32_t kOffBar = kOffKV + kStages * kTileBytes;  // mbarriers
+struct Bars {
+    uint64_t q_full[kQTiles];
+    uint64_t kv_full[kStages];
+    uint64_t kv_empty[kStages];
+    uint64_t s_full[kQTiles];
+    uint64_t p_full[kQTiles];
+    uint64_t o_final;
+    uint32_t tmem_base;
+    int abort;
+};
+constexpr uint32_t kSmemBytes = kOffBar + sizeof(Bars) + 1024;  // + alignment slack
+
+struct AttnArgs {
+    int S;        // sequence length (queries = keys)
+    int BH;       // batch * heads
+    int nqb;      // query blocks of kQTiles * kRows rows per (batch, head)
+    int causal;
+    float sl2;    // scale * log2(e)
+    float* lse;   // [BH, S] natural log-sum-exp, nullable
+};
+
+// Bounded wait on phase `parity` of `bar`. Gives up early when another role has aborted the CTA.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (uint32_t i = 1; i < (1u << 30); ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0) {
+            if (*abort) return false;
+            if (clock64() - t0 > kWaitCycles) break;
+        }
+    }
+    atomicOr(&g_attn_fault, 2u);
+    *abort = 1;
+    return false;
+}
+
+// Bounded wait used while shutting down: ignores the abort flag (outstanding copies and MMAs
+// must land before the CTA exits) but still gives up after the same limit.
+__device__ __forceinline__ void drain_bar(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return;
+    const long long t0 = clock64();
+    for (uint32_t i = 1; i < (1u << 30); ++i) {
+        if (mbar_try_wait(bar, parity)) return;
+        if ((i & 255u) == 0 && clock64() - t0 > kWaitCycles) break;
+    }
+    atomicOr(&g_attn_fault, 2u);
+}
+
+__device__ __forceinline__ void producer(const CUtensorMap* mq, const CUtensorMap* mk, const CUtensorMap* mv,
+                                         uint8_t* smem, Bars* b, int bh, int q0, int n) {
+    volatile int* abort = &b->abort;
+    tc::prefetch_map(mq);
+    tc::prefetch_map(mk);
+    tc::prefetch_map(mv);
+    for (int t = 0; t < kQTiles; ++t) {
+        uint8_t* dst = smem + kOffQ + t * kTileBytes;
+        mbar_expect_tx(&b->q_full[t], kTileBytes);
+        tc::tma_load_3d(dst, mq, 0, q0 + t * kRows, bh, &b->q_full[t]);
+        tc::tma_load_3d(dst + kHalfBytes, mq, kDim / 2, q0 + t * kRows, bh, &b->q_full[t]);
+    }
+    uint32_t issued[kStages] = {};
+    for (int it = 0; it < 2 * n; ++it) {
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        if (!wait_bar(&b->kv_empty[s], ph ^ 1u, abort)) break;
+        uint8_t* dst = smem + kOffKV + s * kTileBytes;
+        const CUtensorMap* m = (it & 1) ? mv : mk;
+        const int row = (it >> 1) * kKeys;
+        mbar_expect_tx(&b->kv_full[s], kTileBytes);
+        tc::tma_load_3d(dst, m, 0, row, bh, &b->kv_full[s]);
+        tc::tma_load_3d(dst + kHalfBytes, m, kDim / 2, row, bh, &b->kv_full[s]);
+        ++issued[s];
+    }
+    // Every copy issued into this CTA's shared memory lands before the CTA may exit.
+    for (int t = 0; t < kQTiles; ++t) drain_bar(&b->q_full[t], 0);
+    for (int s = 0; s < kStages; ++s)
+        if (issued[s]) drain_bar(&b->kv_full[s], (issued[s] - 1) & 1u);
+}
+
+__device__ __forceinline__ void mma_issuer(uint8_t* smem, Bars* b, uint32_t tmem, int n) {
+    volatile int* abort = &b->abort;
+    const uint32_t q_addr = smem_u32(smem + kOffQ);
+    const uint32_t kv_addr = smem_u32(smem + kOffKV);
+    // S_t = Q_t K^T: eight K=16 steps along the head dimension; 32 bytes per step inside a
+    // 128-byte swizzled row, the second 64 columns in the other half tile.
+    auto qk = [&](int t, int s) {
+        const uint32_t qa = q_addr + t * kTileBytes, ka = kv_addr + s * kTileBytes;
+#pragma unroll
+        for (int k = 0; k < kDim / 16; ++k) {
+            const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32;
+            tc::mma_ss(tmem + kColS0 + 128 * t, tc::sw128_desc(qa + off, 16, 1024), tc::sw128_desc(ka + off, 16, 1024),
+                       kIdescQK, k > 0);
+        }
+    };
+    // O_t += P_t V: eight K=16 steps along the keys; P from TMEM (8 columns per step), V as an
+    // MN-major operand (head dimension contiguous, 16 key rows = 2048 bytes per step, the second
+    // 64 head columns 16 KB further).
+    auto pv = [&](int t, int s, bool acc) {
+        const uint32_t va = kv_addr + s * kTileBytes;
+#pragma unroll
+        for (int k = 0; k < kKeys / 16; ++k)
+            tc::mma_ts(tmem + kColO0 + 128 * t, tmem + kColS0 + 128 * t + kColP + 8 * k,
+                       tc::sw128_desc(va + k * 2048, kHalfBytes, 1024), kIdescPV, (acc || k > 0) ? 1u : 0u);
+    };
+    bool ok = wait_bar(&b->q_full[0], 0, abort) && wait_bar(&b->q_full[1], 0, abort) &&
+              wait_bar(&b->kv_full[0], 0, abort);
+    if (ok) {
+        tc::fence_after();
+        qk(0, 0);
+        tc::commit(&b->s_full[0]);
+        qk(1, 0);
+        tc::commit(&b->s_full[1]);
+        tc::commit(&b->kv_empty[0]);
+    }
+    for (int j = 0; ok && j < n; ++j) {
+        const int itv = 2 * j + 1, sv = itv % kStages;
+        const int itk = 2 * j + 2, sk = itk % kStages;
+        const bool more = j + 1 < n;
+        if (!(ok = wait_bar(&b->kv_full[sv], (itv / kStages) & 1u, abort))) break;
+        if (!(ok = wait_bar(&b->p_full[0], j & 1u, abort))) break;
+        tc::fence_after();
+        pv(0, sv, j > 0);
+        if (more) {
+            if (!(ok = wait_bar(&b->kv_full[sk], (itk / kStages) & 1u, abort))) break;
+            tc::fence_after();
+            qk(0, sk);
+            tc::commit(&b->s_full[0]);
+        }
+        if (!(ok = wait_bar(&b->p_full[1], j & 1u, abort))) break;
+        tc::fence_after();
+        pv(1, sv, j > 0);
+        tc::commit(&b->kv_empty[sv]);
+        if (more) {
+            qk(1, sk);
+            tc::commit(&b->s_full[1]);
+            tc::commit(&b->kv_empty[sk]);
+        }
+    }
+    // Arrives when every MMA above has finished (at once if none was issued).
+    tc::commit(&b->o_final);
+    drain_bar(&b->o_final, 0);
+}
+
+__device__ __forceinline__ void softmax_tile(const CUtensorMap* mo, uint8_t* smem, Bars* b, uint32_t tmem,
+                                             const AttnArgs& a, int bh, int q0, int n) {
+    volatile int* abort = &b->abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = warp >> 2, wq = warp & 3;
+    const int r = wq * 32 + lane;  // row inside the tile = TMEM lane
+    const int qrow = q0 + t * kRows + r;
+    const int lim = a.causal ? min(qrow, a.S - 1) : a.S - 1;  // last key this row attends to
+    const uint32_t lanes = (uint32_t)(wq * 32) << 16;
+    const uint32_t tS = tmem + lanes + kColS0 + 128 * t;
+    const uint32_t tP = tS + kColP;
+    const uint32_t tO = tmem + lanes + kColO0 + 128 * t;
+    const float sl2 = a.sl2;
+    float m = -NB200_INF, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+        // All lanes take the same branch: the TMEM accesses below are warp-collective.
+        if (!(ok = __all_sync(0xffffffffu, wait_bar(&b->s_full[t], j & 1u, abort)))) break;
+        tc::fence_after();
+        uint32_t u[128];
+        tc::tmem_ld128(tS, u);
+        float s[128];
+#pragma unroll
+        for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(u[c]);
+        const int kb = j * kKeys;
+        if (kb + kKeys - 1 > lim) {
+#pragma unroll
+            for (int c = 0; c < 128; ++c)
+                if (kb + c > lim) s[c] = -NB200_INF;
+        }
+        float mx[4] = {-NB200_INF, -NB200_INF, -NB200_INF, -NB200_INF};
+#pragma unroll
+        for (int c = 0; c < 128; c += 4) {
+            mx[0] = fmaxf(mx[0], s[c]);
+            mx[1] = fmaxf(mx[1], s[c + 1]);
+            mx[2] = fmaxf(mx[2], s[c + 2]);
+            mx[3] = fmaxf(mx[3], s[c + 3]);
+        }
+        const float mnew = fmaxf(m, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2);
+        const bool grow = mnew > m + kRescaleSlack;
+        if (__any_sync(0xffffffffu, grow)) {
+            // Move the whole warp to the new maxima; rows whose max did not move keep factor 1.
+            const float f = (mnew == m) ? 1.f : ex2(m - mnew);
+            if (j > 0) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t v[32];
+                    tc::tmem_ld32(tO + 32 * c, v);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * f);
+                    tc::tmem_st32(tO + 32 * c, v);
+                }
+            }
+            l *= f;
+            m = mnew;
+        }
+        const float nm = -m;
+        float ls[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float p0 = ex2(fmaf(s[32 * c + 2 * i], sl2, nm));
+                const float p1 = ex2(fmaf(s[32 * c + 2 * i + 1], sl2, nm));
+                ls[(i & 1) * 2] += p0;
+                ls[(i & 1) * 2 + 1] += p1;
+                pk[i] = tc::pack_bf16(p0, p1);
+            }
+            tc::tmem_st16(tP + 16 * c, pk);
+        }
+        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+        tc::tmem_wait_st();
+        tc::fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&b->p_full[t]);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, wait_bar(&b->o_final, 0, abort));
+    if (!ok) return;
+    tc::fence_after();
+    // Epilogue: O / l in bf16, written into this tile's (now idle) Q buffer in the swizzled layout
+    // the O tensor map expects, then one TMA store per warp for its 32 rows.
+    uint8_t* stage = smem + kOffQ + t * kTileBytes;
+    const float inv = 1.f / l;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tc::tmem_ld32(tO + 32 * c, v);
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            pk[i] = tc::pack_bf16(__uint_as_float(v[2 * i]) * inv, __uint_as_float(v[2 * i + 1]) * inv);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int ch = 4 * c + q;  // 16-byte chunk of the 256-byte row
+            uint8_t* dst = stage + (ch >> 3) * kHalfBytes + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        }
+    }
+    if (a.lse && qrow < a.S) a.lse[(size_t)bh * a.S + qrow] = (m + log2f(l)) * 0.69314718055994531f;
+    fence_proxy_async();
+    __syncwarp();
+    const int row0 = q0 + t * kRows + wq * 32;
+    if (lane == 0 && row0 < a.S) {
+        tc::tma_store_3d(mo, stage + wq * 32 * 128, 0, row0, bh);
+        tc::tma_store_3d(mo, stage + kHalfBytes + wq * 32 * 128, kDim / 2, row0, bh);
+        tc::bulk_commit();
+        tc::bulk_wait_read();
+    }
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+                    const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mo, AttnArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Bars* b = reinterpret_cast<Bars*>(smem + kOffBar);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // Causal work shrinks with the query block: hand out the longest blocks first.
+    const int qb = a.nqb - 1 - (int)(blockIdx.x / (unsigned)a.BH);
+    const int bh = (int)(blockIdx.x % (unsigned)a.BH);
+    const int q0 = qb * kQTiles * kRows;
+    const int kv_end = a.causal ? min(q0 + kQTiles * kRows, a.S) : a.S;
+    const int n = (kv_end + kKeys - 1) / kKeys;
+
+    if (threadIdx.x == 0) {
+        for (int t = 0; t < kQTiles; ++t) {
+            mbar_init(&b->q_full[t], 1);
+            mbar_init(&b->s_full[t], 1);
+            mbar_init(&b->p_full[t], 4);  // one arrival per softmax warp
+        }
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&b->kv_full[s], 1);
+            mbar_init(&b->kv_empty[s], 1);
+        }
+        mbar_init(&b->o_final, 1);
+        b->abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == kMmaWarp) {
+        tc::tmem_alloc(&b->tmem_base, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tmem = b->tmem_base;
+
+    if (warp == kLoadWarp) {
+        if (lane == 0) producer(&mq, &mk, &mv, smem, b, bh, q0, n);
+        __syncwarp();
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) mma_issuer(smem, b, tmem, n);
+        __syncwarp();
+    } else {
+        softmax_tile(&mo, smem, b, tmem, a, bh, q0, n);
+    }
+    tc::fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc::fence_after();
+        tc::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+std::mutex g_attr_mutex;
+bool g_attr_set[64] = {false};
+
+int get_encoder() {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+        cudaGetLastError();
+    });
+    if (!g_encode) {
+        set_error("nb200_attention: the driver does not provide cuTensorMapEncodeTiled");
+        return NB200_ERR_LAUNCH;
+    }
+    return NB200_OK;
+}
+
+// [BH, S, D] bf16 viewed as a 3-D tensor map with a {64, box_rows, 1} box and 128-byte swizzle.
+int encode_map(CUtensorMap* map, const void* base, int64_t BH, int64_t S, uint32_t box_rows, const char* what) {
+    const cuuint64_t dims[3] = {(cuuint64_t)kDim, (cuuint64_t)S, (cuuint64_t)BH};
+    const cuuint64_t strides[2] = {(cuuint64_t)kDim * 2, (cuuint64_t)S * kDim * 2};
+    const cuuint32_t box[3] = {kDim / 2, box_rows, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult rc = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides,
+                                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (rc != CUDA_SUCCESS) {
+        set_error("nb200_attention: cannot describe %s as a tensor map (CUresult %d)", what, (int)rc);
+        return NB200_ERR_ARG;
+    }
+    return NB200_OK;
+}
+
+}  // namespace
+
+int attn_fault_take(unsigned int* bits) {
+    unsigned int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_attn_fault, sizeof(v)) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_attn_fault, &zero, sizeof(zero)) != cudaSuccess) {
+        set_error("cannot read the attention fault word: %s", cudaGetErrorString(cudaGetLastError()));
+        return NB200_ERR_LAUNCH;
+    }
+    *bits = v;
+    return NB200_OK;
+}
+
+int launch_attention(const void* q, const void* k, const void* v, void* o, float* lse, int64_t B, int64_t H,
+                     int64_t S, int64_t D, int causal, float scale, cudaStream_t st) {
+    if (D != kDim) {
+        set_error("nb200_attention: head_dim %lld is not supported (this kernel is built for %d)", (long long)D, kDim);
+        return NB200_ERR_UNSUPPORTED;
+    }
+    if (!(scale > 0.f)) {
+        set_error("nb200_attention: scale must be positive");
+        return NB200_ERR_ARG;
+    }
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) ||
+        (lse && (reinterpret_cast<uintptr_t>(lse) & 3u))) {
+        set_error("nb200_attention: q, k, v, o must be 16-byte aligned and lse 4-byte aligned");
+        return NB200_ERR_ARG;
+    }
+    const int64_t BH = B * H;
+    const int64_t nqb = (S + kQTiles * kRows - 1) / (kQTiles * kRows);
+    if (S > (int64_t)1 << 30 || BH > (int64_t)1 << 30 || BH * nqb > 0x7fffffffLL) {
+        set_error("nb200_attention: batch*heads=%lld, seq=%lld exceed the kernel's index range", (long long)BH,
+                  (long long)S);
+        return NB200_ERR_CAPACITY;
+    }
+    int rc = get_encoder();
+    if (rc) return rc;
+    CUtensorMap mq, mk, mv, mo;
+    if ((rc = encode_map(&mq, q, BH, S, kRows, "q")) || (rc = encode_map(&mk, k, BH, S, kKeys, "k")) ||
+        (rc = encode_map(&mv, v, BH, S, kKeys, "v")) || (rc = encode_map(&mo, o, BH, S, 32, "o")))
+        return rc;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        set_error("nb200_attention: no usable current CUDA device");
+        return NB200_ERR_LAUNCH;
+    }
+    {
+        std::lock_guard<std::mutex> lock(g_attr_mutex);
+        if (!g_attr_set[dev]) {
+            if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
+                cudaSuccess) {
+                set_error("nb200_attention: cannot reserve %u bytes of shared memory: %s", kSmemBytes,
+                          cudaGetErrorString(cudaGetLastError()));
+                return NB200_ERR_LAUNCH;
+            }
+            g_attr_set[dev] = true;
+        }
+    }
+    AttnArgs a;
+    a.S = (int)S;
+    a.BH = (int)BH;
+    a.nqb = (int)nqb;
+    a.causal = causal ? 1 : 0;
+    a.sl2 = scale * 1.4426950408889634f;
+    a.lse = lse;
+    attn_fwd_kernel<<<(unsigned)(BH * nqb), kThreads, kSmemBytes, st>>>(mq, mk, mv, mo, a);
+    count_launch();
+    return finish_launch("nb200_attention");
 }
 
 }  // namespace nb200

@@ -122,9 +122,10 @@ uint64_t nb200_launch_count(void) { return g_launches.load(std::memory_order_rel
 
 int nb200_stream_fault(uint32_t* bits) {
     if (!bits) { set_error("nb200_stream_fault: null pointer"); return NB200_ERR_ARG; }
-    unsigned int v = 0;
-    const int rc = stream_fault_take(&v);
-    *bits = v;
+    unsigned int v = 0, w = 0;
+    int rc = stream_fault_take(&v);
+    if (rc == NB200_OK) rc = attn_fault_take(&w);
+    *bits = v | w;
     return rc;
 }
 

@@ -48,6 +48,7 @@ int stream_span(int sk, const Params& p, const void* x, int dtype, int64_t rows,
                 int64_t srow, int64_t scol, int64_t cc, int64_t nparts, nb200_state* states, void* out,
                 int finalize, const nb200_launch* L, cudaStream_t st);
 int stream_fault_take(unsigned int* bits);
+int attn_fault_take(unsigned int* bits);
 
 int launch_attention(const void* q, const void* k, const void* v, void* o, float* lse,
                      int64_t B, int64_t H, int64_t S, int64_t D, int causal, float scale,

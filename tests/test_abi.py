@@ -75,6 +75,17 @@ def test_argument_validation_happens_before_any_launch():
     assert lib.nb200_segment_pool(null, 0, 1, 1, 1, 1, null, 1, 1, 1, 7, 0, 0, null, null, null) == L.NB200_ERR_ARG
     assert lib.nb200_segment_pool(null, 0, 1, 1, 1, 1, null, 9, 1, 1, 0, 0, 0, null, null, null) == L.NB200_ERR_ARG
     assert lib.nb200_segment_pool(null, 0, 1, 4, 4, 1, null, 1, 1, 0, 0, 0, 0, null, null, null) == L.NB200_OK
+    # attention: shape, head_dim, scale and alignment are refused on the host (the pointers are
+    # never dereferenced); an empty problem is a successful no-op
+    fake = ctypes.c_void_p(1 << 20)
+    assert lib.nb200_attention(null, null, null, null, None, 1, 1, 0, 128, 0, 0.1, null) == L.NB200_OK
+    assert lib.nb200_attention(null, fake, fake, fake, None, 1, 1, 8, 128, 0, 0.1, null) == L.NB200_ERR_ARG
+    assert lib.nb200_attention(fake, fake, fake, fake, None, 1, 1, 8, 64, 0, 0.1, null) == L.NB200_ERR_UNSUPPORTED
+    assert "head_dim" in L.last_error()
+    assert lib.nb200_attention(fake, fake, fake, fake, None, 1, 1, 8, 128, 0, -1.0, null) == L.NB200_ERR_ARG
+    odd = ctypes.c_void_p((1 << 20) + 2)
+    assert lib.nb200_attention(odd, fake, fake, fake, None, 1, 1, 8, 128, 1, 0.1, null) == L.NB200_ERR_ARG
+    assert "aligned" in L.last_error()
 
 
 def test_check_maps_status_to_reference_exceptions():
