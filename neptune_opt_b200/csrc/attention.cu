@@ -44,12 +44,19 @@ constexpr int kRows = 128;   // query rows per tile (= TMEM lanes)
 constexpr int kQTiles = 2;   // query tiles per CTA
 constexpr int kKeys = 128;   // keys per K/V tile
 constexpr int kDim = 128;    // head dimension
-constexpr int kStages = 4;   // K/V ring stages; each holds one K or one V tile
+constexpr int kStages = 5;   // K/V ring stages; each holds one K or one V tile
 constexpr uint32_t kTileBytes = kRows * kDim * 2;  // 32 KB per Q, K or V tile
 constexpr uint32_t kHalfBytes = kTileBytes / 2;    // one 64-column half: the TMA box
 constexpr int kMmaWarp = 8;
 constexpr int kLoadWarp = 9;
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;  // warps 10-11 only complete the third warpgroup for the register split
+// Register split (setmaxnreg, per warpgroup): the softmax warpgroups hold a 128-column score row
+// per thread; the MMA/producer warpgroup needs little. The sum stays within what the block is
+// launched with (kThreads x kLaunchRegs), so the increase never waits on registers that do not exist.
+constexpr int kLaunchRegs = 168;
+constexpr int kRegsSoftmax = 216;
+constexpr int kRegsControl = 72;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsControl <= kThreads * kLaunchRegs, "register split");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS0 = 0, kColO0 = 256;  // tile t: S at kColS0 + 128 t, O at kColO0 + 128 t
 constexpr uint32_t kColP = 64;                // P inside S's columns
@@ -67,7 +74,7 @@ struct Bars {
     uint64_t kv_full[kStages];
     uint64_t kv_empty[kStages];
     uint64_t s_full[kQTiles];
-    uint64_t p_full[kQTiles];
+    uint64_t p_full[kQTiles][2];  // per half of P (keys 0-63, 64-127)
     uint64_t o_final;
     uint32_t tmem_base;
     int abort;
@@ -111,6 +118,94 @@ __device__ __forceinline__ void drain_bar(uint64_t* bar, uint32_t parity) {
     atomicOr(&g_attn_fault, 2u);
 }
 
+// ------------------------------------------------------------------ softmax arithmetic
+// Pairs of fp32 values in one 64-bit register, for the sm_100 packed f32x2 instructions.
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+    return (uint64_t)__float_as_uint(lo) | ((uint64_t)__float_as_uint(hi) << 32);
+}
+__device__ __forceinline__ float f2lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+// 2^x on the special-function unit; subnormal results flush to zero (they are far below a bf16
+// probability's resolution next to the row maximum's 1).
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// 2^x for a pair on the FMA pipe, to take part of the exponentials off the special-function unit.
+// Cody-Waite style range reduction x = j + f with j = round(x) (adding and subtracting 1.5 * 2^23
+// rounds to an integer in the low mantissa bits of t) and f in [-1/2, 1/2]; 2^f from a degree-4
+// polynomial fitted here for minimum relative error on [-1/2, 1/2] (max relative error 2.6e-6:
+// far below a bf16 probability's 2^-9 rounding, and small enough that the row sums, hence the
+// log-sum-exp, keep fp32-level accuracy); 2^j is added to the exponent field as j << 23,
+// which the integer multiply-add bits(t) * 2^23 + bits(2^f) produces because bits(t) = 0x4B400000
+// + j and 0x4B400000 * 2^23 vanishes mod 2^32. x must be >= -126 (the caller clamps).
+constexpr float kPolyC0 = 0.9999992847442627f, kPolyC1 = 0.6931217908859253f;
+constexpr float kPolyC2 = 0.2402474582195282f, kPolyC3 = 0.05591786280274391f;
+constexpr float kPolyC4 = 0.00957004725933075f;
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
+    const float magic = 12582912.f;  // 1.5 * 2^23
+    const uint64_t t = add2(x, f2(magic, magic));
+    const uint64_t jf = add2(t, f2(-magic, -magic));
+    const uint64_t f = fma2(jf, f2(-1.f, -1.f), x);
+    uint64_t p = fma2(f2(kPolyC4, kPolyC4), f, f2(kPolyC3, kPolyC3));
+    p = fma2(p, f, f2(kPolyC2, kPolyC2));
+    p = fma2(p, f, f2(kPolyC1, kPolyC1));
+    p = fma2(p, f, f2(kPolyC0, kPolyC0));
+    const uint32_t lo = (uint32_t)t * 0x800000u + (uint32_t)p;
+    const uint32_t hi = (uint32_t)(t >> 32) * 0x800000u + (uint32_t)(p >> 32);
+    return (uint64_t)lo | ((uint64_t)hi << 32);
+}
+
+// Of every 8 key pairs, kPolyPer8 take the polynomial path (spread evenly), the rest ex2.
+constexpr int kPolyPer8 = 3;
+constexpr bool poly_pair(int i) { return kPolyPer8 > 0 && ((i & 7) * kPolyPer8) % 8 < kPolyPer8; }
+
+// P for keys [64 h, 64 h + 64) of this row: p = 2^(s * sl2 - m) rounded to bf16 into TMEM
+// (one column per key pair, the lower key in the low half), fp32 p added to the row sums.
+// Masked tiles (some key past the row's last) use the special-function unit for every pair:
+// their -inf scores would need the polynomial's clamp anyway.
+template <bool kMasked>
+__device__ __forceinline__ void p_half(const float* s, int h, uint64_t sl2, uint64_t nm, uint64_t& acc0,
+                                       uint64_t& acc1, uint32_t tP) {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const int pi = 32 * h + 16 * c + i;
+            const uint64_t x = fma2(f2(s[2 * pi], s[2 * pi + 1]), sl2, nm);
+            uint64_t p;
+            if (!kMasked && poly_pair(pi))
+                p = exp2_poly2(f2(fmaxf(f2lo(x), -126.f), fmaxf(f2hi(x), -126.f)));
+            else
+                p = f2(ex2_ftz(f2lo(x)), ex2_ftz(f2hi(x)));
+            if (i & 1)
+                acc1 = add2(acc1, p);
+            else
+                acc0 = add2(acc0, p);
+            pk[i] = tc::pack_bf16(f2lo(p), f2hi(p));
+        }
+        tc::tmem_st16(tP + 32 * h + 16 * c, pk);
+    }
+}
+
 __device__ __forceinline__ void producer(const CUtensorMap* mq, const CUtensorMap* mk, const CUtensorMap* mv,
                                          uint8_t* smem, Bars* b, int bh, int q0, int n) {
     volatile int* abort = &b->abort;
@@ -123,8 +218,8 @@ __device__ __forceinline__ void producer(const CUtensorMap* mq, const CUtensorMa
         tc::tma_load_3d(dst, mq, 0, q0 + t * kRows, bh, &b->q_full[t]);
         tc::tma_load_3d(dst + kHalfBytes, mq, kDim / 2, q0 + t * kRows, bh, &b->q_full[t]);
     }
-    uint32_t issued[kStages] = {};
-    for (int it = 0; it < 2 * n; ++it) {
+    int it = 0;
+    for (; it < 2 * n; ++it) {
         const int s = it % kStages;
         const uint32_t ph = (it / kStages) & 1;
         if (!wait_bar(&b->kv_empty[s], ph ^ 1u, abort)) break;
@@ -134,12 +229,12 @@ __device__ __forceinline__ void producer(const CUtensorMap* mq, const CUtensorMa
         mbar_expect_tx(&b->kv_full[s], kTileBytes);
         tc::tma_load_3d(dst, m, 0, row, bh, &b->kv_full[s]);
         tc::tma_load_3d(dst + kHalfBytes, m, kDim / 2, row, bh, &b->kv_full[s]);
-        ++issued[s];
     }
-    // Every copy issued into this CTA's shared memory lands before the CTA may exit.
+    // Every copy issued into this CTA's shared memory lands before the CTA may exit: wait for the
+    // last phase filled in each stage (`it` tiles were issued, stage s got those with index = s
+    // mod kStages).
     for (int t = 0; t < kQTiles; ++t) drain_bar(&b->q_full[t], 0);
-    for (int s = 0; s < kStages; ++s)
-        if (issued[s]) drain_bar(&b->kv_full[s], (issued[s] - 1) & 1u);
+    for (int s = 0; s < kStages && s < it; ++s) drain_bar(&b->kv_full[s], ((it - 1 - s) / kStages) & 1u);
 }
 
 __device__ __forceinline__ void mma_issuer(uint8_t* smem, Bars* b, uint32_t tmem, int n) {
@@ -160,12 +255,21 @@ __device__ __forceinline__ void mma_issuer(uint8_t* smem, Bars* b, uint32_t tmem
     // O_t += P_t V: eight K=16 steps along the keys; P from TMEM (8 columns per step), V as an
     // MN-major operand (head dimension contiguous, 16 key rows = 2048 bytes per step, the second
     // 64 head columns 16 KB further).
-    auto pv = [&](int t, int s, bool acc) {
+    // Issued in two halves of 64 keys, each as soon as the softmax warps publish that half of P.
+    auto pv = [&](int t, int s, int h, bool acc) {
         const uint32_t va = kv_addr + s * kTileBytes;
 #pragma unroll
-        for (int k = 0; k < kKeys / 16; ++k)
+        for (int k = 4 * h; k < 4 * h + 4; ++k)
             tc::mma_ts(tmem + kColO0 + 128 * t, tmem + kColS0 + 128 * t + kColP + 8 * k,
                        tc::sw128_desc(va + k * 2048, kHalfBytes, 1024), kIdescPV, (acc || k > 0) ? 1u : 0u);
+    };
+    auto pv_tile = [&](int t, int s, bool acc, uint32_t parity) {
+        for (int h = 0; h < 2; ++h) {
+            if (!wait_bar(&b->p_full[t][h], parity, abort)) return false;
+            tc::fence_after();
+            pv(t, s, h, acc);
+        }
+        return true;
     };
     bool ok = wait_bar(&b->q_full[0], 0, abort) && wait_bar(&b->q_full[1], 0, abort) &&
               wait_bar(&b->kv_full[0], 0, abort);
@@ -182,18 +286,14 @@ __device__ __forceinline__ void mma_issuer(uint8_t* smem, Bars* b, uint32_t tmem
         const int itk = 2 * j + 2, sk = itk % kStages;
         const bool more = j + 1 < n;
         if (!(ok = wait_bar(&b->kv_full[sv], (itv / kStages) & 1u, abort))) break;
-        if (!(ok = wait_bar(&b->p_full[0], j & 1u, abort))) break;
-        tc::fence_after();
-        pv(0, sv, j > 0);
+        if (!(ok = pv_tile(0, sv, j > 0, j & 1u))) break;
         if (more) {
             if (!(ok = wait_bar(&b->kv_full[sk], (itk / kStages) & 1u, abort))) break;
             tc::fence_after();
             qk(0, sk);
             tc::commit(&b->s_full[0]);
         }
-        if (!(ok = wait_bar(&b->p_full[1], j & 1u, abort))) break;
-        tc::fence_after();
-        pv(1, sv, j > 0);
+        if (!(ok = pv_tile(1, sv, j > 0, j & 1u))) break;
         tc::commit(&b->kv_empty[sv]);
         if (more) {
             qk(1, sk);
@@ -231,20 +331,24 @@ __device__ __forceinline__ void softmax_tile(const CUtensorMap* mo, uint8_t* sme
 #pragma unroll
         for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(u[c]);
         const int kb = j * kKeys;
-        if (kb + kKeys - 1 > lim) {
+        // Warp-uniform: the tile holds a key past some row's last (causal diagonal, ragged end).
+        const bool masked = __any_sync(0xffffffffu, kb + kKeys - 1 > lim);
+        if (masked) {
 #pragma unroll
             for (int c = 0; c < 128; ++c)
                 if (kb + c > lim) s[c] = -NB200_INF;
         }
-        float mx[4] = {-NB200_INF, -NB200_INF, -NB200_INF, -NB200_INF};
+        float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
 #pragma unroll
-        for (int c = 0; c < 128; c += 4) {
-            mx[0] = fmaxf(mx[0], s[c]);
-            mx[1] = fmaxf(mx[1], s[c + 1]);
-            mx[2] = fmaxf(mx[2], s[c + 2]);
-            mx[3] = fmaxf(mx[3], s[c + 3]);
+        for (int c = 4; c < 124; c += 8) {
+            a0 = max3(a0, s[c], s[c + 1]);
+            a1 = max3(a1, s[c + 2], s[c + 3]);
+            a2 = max3(a2, s[c + 4], s[c + 5]);
+            a3 = max3(a3, s[c + 6], s[c + 7]);
         }
-        const float mnew = fmaxf(m, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * sl2);
+        a0 = max3(a0, s[124], s[125]);
+        a1 = max3(a1, s[126], s[127]);
+        const float mnew = fmaxf(m, fmaxf(max3(a0, a1, a2), a3) * sl2);
         const bool grow = mnew > m + kRescaleSlack;
         if (__any_sync(0xffffffffu, grow)) {
             // Move the whole warp to the new maxima; rows whose max did not move keep factor 1.
@@ -262,26 +366,21 @@ __device__ __forceinline__ void softmax_tile(const CUtensorMap* mo, uint8_t* sme
             l *= f;
             m = mnew;
         }
-        const float nm = -m;
-        float ls[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint64_t sl2x2 = f2(sl2, sl2), nm = f2(-m, -m);
+        uint64_t acc0 = 0, acc1 = 0;  // packed fp32 partial row sums (+0.0 bit patterns)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            uint32_t pk[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const float p0 = ex2(fmaf(s[32 * c + 2 * i], sl2, nm));
-                const float p1 = ex2(fmaf(s[32 * c + 2 * i + 1], sl2, nm));
-                ls[(i & 1) * 2] += p0;
-                ls[(i & 1) * 2 + 1] += p1;
-                pk[i] = tc::pack_bf16(p0, p1);
-            }
-            tc::tmem_st16(tP + 16 * c, pk);
+        for (int h = 0; h < 2; ++h) {
+            if (masked)
+                p_half<true>(s, h, sl2x2, nm, acc0, acc1, tP);
+            else
+                p_half<false>(s, h, sl2x2, nm, acc0, acc1, tP);
+            tc::tmem_wait_st();
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&b->p_full[t][h]);
         }
-        l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-        tc::tmem_wait_st();
-        tc::fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&b->p_full[t]);
+        const uint64_t acc = add2(acc0, acc1);
+        l += f2lo(acc) + f2hi(acc);
     }
     if (ok) ok = __all_sync(0xffffffffu, wait_bar(&b->o_final, 0, abort));
     if (!ok) return;
@@ -326,9 +425,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     Bars* b = reinterpret_cast<Bars*>(smem + kOffBar);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    // Causal work shrinks with the query block: hand out the longest blocks first.
-    const int qb = a.nqb - 1 - (int)(blockIdx.x / (unsigned)a.BH);
-    const int bh = (int)(blockIdx.x % (unsigned)a.BH);
+    // Head-major order: the query blocks of one (batch, head) run side by side and share its K/V
+    // through L2, so each head's K/V is read from HBM about once. Within a head the longest causal
+    // blocks go first.
+    const int bh = (int)(blockIdx.x / (unsigned)a.nqb);
+    const int qb = a.nqb - 1 - (int)(blockIdx.x % (unsigned)a.nqb);
     const int q0 = qb * kQTiles * kRows;
     const int kv_end = a.causal ? min(q0 + kQTiles * kRows, a.S) : a.S;
     const int n = (kv_end + kKeys - 1) / kKeys;
@@ -337,7 +438,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < kQTiles; ++t) {
             mbar_init(&b->q_full[t], 1);
             mbar_init(&b->s_full[t], 1);
-            mbar_init(&b->p_full[t], 4);  // one arrival per softmax warp
+            mbar_init(&b->p_full[t][0], 4);  // one arrival per softmax warp
+            mbar_init(&b->p_full[t][1], 4);
         }
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&b->kv_full[s], 1);
@@ -356,20 +458,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::fence_after();
     const uint32_t tmem = b->tmem_base;
 
-    if (warp == kLoadWarp) {
-        if (lane == 0) producer(&mq, &mk, &mv, smem, b, bh, q0, n);
-        __syncwarp();
-    } else if (warp == kMmaWarp) {
-        if (lane == 0) mma_issuer(smem, b, tmem, n);
-        __syncwarp();
-    } else {
+    // Each role runs to the end of the kernel in its own branch (the register budget differs per
+    // branch); both end at barrier 0, after which the MMA warp frees the tensor memory.
+    if (warp < 8) {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
         softmax_tile(&mo, smem, b, tmem, a, bh, q0, n);
-    }
-    tc::fence_before();
-    __syncthreads();
-    if (warp == kMmaWarp) {
-        tc::fence_after();
-        tc::tmem_dealloc(tmem, kTmemCols);
+        tc::fence_before();
+        asm volatile("bar.sync 0;" ::: "memory");
+    } else {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+        if (warp == kLoadWarp) {
+            if (lane == 0) producer(&mq, &mk, &mv, smem, b, bh, q0, n);
+            __syncwarp();
+        } else if (warp == kMmaWarp) {
+            if (lane == 0) mma_issuer(smem, b, tmem, n);
+            __syncwarp();
+        }
+        tc::fence_before();
+        asm volatile("bar.sync 0;" ::: "memory");
+        if (warp == kMmaWarp) {
+            tc::fence_after();
+            tc::tmem_dealloc(tmem, kTmemCols);
+        }
     }
 }
 
