@@ -10,7 +10,8 @@ one step = one fused RMSNorm pass over the batch. Every rank processes its own f
 independent, no data-path collective): weak scaling, `value` = all ranks' algorithmic bytes / the
 max-over-ranks step time. The other configs are measured after the headline and reported under
 `regions` (softmax+logsumexp fp32, L2-normalize fp16, split-plan logsumexp bf16, ordered segment
-sum/mean fp16), each with its own roofline fraction.
+sum/mean fp16, and the fused tcgen05 attention bf16 [8,32,4096,128] non-causal and causal in
+TFLOP/s against the measured bf16 tensor peak), each with its own roofline fraction.
 
 Algorithmic bytes count every tensor once (inputs read + outputs written). Between timed steps the
 inputs rotate over buffer sets whose total exceeds the 126 MB L2, so no step reads data a previous
@@ -51,8 +52,12 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--region", default=None,
                     help="time one region only (rms_norm, softmax_lse, logsumexp, l2_normalize, "
-                         "wide_logsumexp_split, segment_sum, segment_mean) and print its line; "
+                         "wide_logsumexp_split, segment_sum, segment_mean, attention, attention_causal) "
+                         "and print its line; "
                          "used for ncu captures of a single kernel")
+    ap.add_argument("--attention-batch", type=int, default=8,
+                    help="batch of the attention regions (8 = the benchmark configuration; smaller "
+                         "values only for profiler captures)")
     return ap.parse_args()
 
 
@@ -61,8 +66,10 @@ def load_peaks():
     if os.path.exists(path):
         with open(path) as f:
             p = json.load(f)
-        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 def profile_traffic(kernel_tag: str):
@@ -303,6 +310,25 @@ def make_segments(torch, NB, seed, reduce="sum"):
             "desc": f"ordered segment_{reduce} fp16 data[{T},{channels}], {nseg} segments Poisson(20) in [1,200], int64 offsets"}
 
 
+def make_attention(torch, NB, seed, causal=False, batch=8):
+    b, h, s, d = batch, 32, 4096, 128
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q, k, v = (torch.randn(b, h, s, d, device="cuda", dtype=torch.bfloat16, generator=g) for _ in range(3))
+    o = torch.empty_like(q)
+    lse = torch.empty(b, h, s, device="cuda", dtype=torch.float32)
+    from neptune_opt_b200.attention import launch_attention
+
+    def step(_i):
+        launch_attention(q, k, v, o, lse, causal=causal, scale=1.0 / d ** 0.5)
+
+    pairs = s * s if not causal else s * (s + 1) // 2  # (query, key) pairs attended per head
+    name = "attention_causal" if causal else "attention"
+    return {"name": name, "step": step, "flops": 4 * b * h * d * pairs, "rows": b * h * s, "launches": 1,
+            "bytes": 4 * b * h * s * d * 2 + b * h * s * 4, "buffers": 1,
+            "desc": f"attention bf16 q,k,v[{b},{h},{s},{d}] N(0,1), scale 1/sqrt({d}), "
+                    f"{'causal' if causal else 'non-causal'} -> o bf16, lse fp32 (inputs {3 * b * h * s * d * 2 >> 20} MiB > L2)"}
+
+
 def gpu_id(torch) -> str:
     """nvidia-smi id of the current device (PCI bus id when torch exposes it)."""
     props = torch.cuda.get_device_properties(torch.cuda.current_device())
@@ -352,6 +378,13 @@ def time_steps(torch, dist, step, steps, warmup, graph=True):
     ms = start.elapsed_time(end) / steps
     del g
     return dist.max(ms), launches
+
+
+def tensor_roofline(flops_per_launch, ms, peaks, traffic):
+    achieved = flops_per_launch / (ms * 1e-3) / 1e12
+    return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": round(achieved / peaks["bf16_tflops"], 4),
+            "peak_source": peaks["source"] + " (burst cuBLAS bf16 GEMM)", "traffic": traffic}
 
 
 def roofline(bytes_per_launch, ms, peaks, traffic):
@@ -429,17 +462,25 @@ REGION_MAKERS = {
     "wide_logsumexp_split": make_wide_lse,
     "segment_sum": lambda t, nb, s: make_segments(t, nb, s, "sum"),
     "segment_mean": lambda t, nb, s: make_segments(t, nb, s, "mean"),
+    "attention": make_attention,
+    "attention_causal": lambda t, nb, s, **kw: make_attention(t, nb, s, causal=True, **kw),
 }
+REGION_OPTIONS = {"attention": ("attention_batch", "batch"), "attention_causal": ("attention_batch", "batch")}
 
 
 def run_region(args, torch, NB, dist, peaks):
-    r = REGION_MAKERS[args.region](torch, NB, 3000 + dist.rank)
+    kw = {}
+    if args.region in REGION_OPTIONS:
+        arg, key = REGION_OPTIONS[args.region]
+        kw[key] = getattr(args, arg)
+    r = REGION_MAKERS[args.region](torch, NB, 3000 + dist.rank, **kw)
     ms, launches = time_steps(torch, dist, r["step"], args.steps, max(3, args.warmup), graph=False)
     if dist.rank == 0:
+        roof = (tensor_roofline(r["flops"], ms, peaks, None) if "flops" in r
+                else roofline(r["bytes"] / r["launches"], ms / r["launches"], peaks, None))
         print(json.dumps({"region": r["name"], "workload": r["desc"], "ms_per_step": round(ms, 5),
                           "GB_per_s": round(dist.world * r["bytes"] / (ms * 1e-3) / 1e9, 1),
-                          "roofline": roofline(r["bytes"] / r["launches"], ms / r["launches"], peaks, None),
-                          "gpu_launches": launches}), flush=True)
+                          "roofline": roof, "gpu_launches": launches}), flush=True)
     dist.close()
     return 0
 
@@ -508,6 +549,27 @@ def main():
                 "algorithmic_bytes_per_step": r["bytes"], "launches_per_step": r["launches"],
                 "traffic_bytes_per_launch": profile_traffic(r["name"]),
                 "l2_rotation_buffers": r["buffers"]}
+            del r
+            torch.cuda.empty_cache()
+        for causal in (False, True):
+            # Burst: 10 launches (~20 ms), the regime of the burst GEMM peak. Sustained: 100
+            # launches back to back (~0.2 s under the power cap), against the sustained peak.
+            r = make_attention(torch, NB, 2500 + dist.rank, causal=causal)
+            ams, _ = time_steps(torch, dist, r["step"], 10, max(3, args.warmup))
+            sms, _ = time_steps(torch, dist, r["step"], 100, 3)
+            sus = tensor_roofline(r["flops"], sms, peaks, None)
+            sus["peak"] = peaks["bf16_tflops_sustained"]
+            sus["frac"] = round(sus["achieved"] / sus["peak"], 4)
+            sus["peak_source"] = peaks["source"] + " (sustained cuBLAS bf16 GEMM under the power cap)"
+            regions[r["name"]] = {
+                "workload": r["desc"], "ms_per_step": round(ams, 5), "steps": 10,
+                "TFLOP_per_s": round(n * r["flops"] / (ams * 1e-3) / 1e12, 1),
+                "rows_per_s": round(n * r["rows"] / (ams * 1e-3), 1),
+                "flops_per_step": r["flops"],
+                "roofline": tensor_roofline(r["flops"], ams, peaks, profile_traffic(r["name"])),
+                "sustained": {"steps": 100, "ms_per_step": round(sms, 5),
+                              "TFLOP_per_s": round(n * r["flops"] / (sms * 1e-3) / 1e12, 1), "roofline": sus},
+                "parallelism": f"heads: each of {n} GPU(s) runs its own [8,32,4096,128] batch"}
             del r
             torch.cuda.empty_cache()
     clocks = sampler.stop() if sampler else None

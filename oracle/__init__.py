@@ -174,3 +174,28 @@ def segment_pool(data, spans, reduce: str, initial, dtype: str) -> np.ndarray:
     lib().oracle_segment_pool(data2, nrows, channels, spans, nseg, 1 if reduce == "mean" else 0, int(has),
                               float(initial) if has else 0.0, DTYPE_CODES[dtype], out)
     return out.reshape((nseg,) + data.shape[1:])
+
+
+def attention(q, k, v, causal=False, scale=None):
+    """fp64 O = softmax(scale * q k^T [+ causal mask]) v and the natural log-sum-exp per query row.
+
+    q, k, v: arrays [..., S, D] (values of bf16 tensors, any float dtype). The causal mask keeps
+    key index <= query index (torch.nn.functional.scaled_dot_product_attention's is_causal for
+    equal query and key lengths); scale defaults to 1/sqrt(D). The reference has no attention
+    kernel, so this unfused float64 computation is the checker for the fused one; its agreement
+    with torch's own CPU scaled_dot_product_attention is pinned in tests/test_oracle_golden.py.
+    """
+    q = np.asarray(q, dtype=np.float64)
+    k = np.asarray(k, dtype=np.float64)
+    v = np.asarray(v, dtype=np.float64)
+    d = q.shape[-1]
+    sc = 1.0 / np.sqrt(d) if scale is None else float(scale)
+    s = np.einsum("...qd,...kd->...qk", q, k) * sc
+    if causal:
+        n = s.shape[-1]
+        s = np.where(np.triu(np.ones((n, n), dtype=bool), 1), -np.inf, s)
+    m = s.max(axis=-1, keepdims=True)
+    e = np.exp(s - m)
+    tot = e.sum(axis=-1, keepdims=True)
+    o = np.einsum("...qk,...kd->...qd", e / tot, v)
+    return o, (m + np.log(tot))[..., 0]

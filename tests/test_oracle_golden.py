@@ -139,3 +139,20 @@ def test_round_dtype_matches_torch_rtne(oracle_mod):
                         np.array([65504, 65519.99, 65520, 1e-40, -0.0, 6e-8, 3e38, -3.4e38], np.float32)])
     for dtype in ("bfloat16", "float16"):
         np.testing.assert_array_equal(oracle_mod.round_dtype(x, dtype), round_to(x, dtype))
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_oracle_agrees_with_torch_sdpa_on_cpu(causal):
+    """The fp64 attention checker against torch's own CPU scaled_dot_product_attention (math
+    backend, float64) on bf16-valued inputs, including a ragged length."""
+    import torch
+
+    import oracle
+
+    gen = torch.Generator().manual_seed(11)
+    for s in (1, 37, 130):
+        q, k, v = (torch.randn(2, 3, s, 128, generator=gen).to(torch.bfloat16).double() for _ in range(3))
+        want = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=causal).numpy()
+        got, lse = oracle.attention(q.numpy(), k.numpy(), v.numpy(), causal=causal)
+        np.testing.assert_allclose(got, want, rtol=1e-10, atol=1e-12)
+        assert lse.shape == (2, 3, s) and np.all(np.isfinite(lse))
