@@ -91,6 +91,8 @@ struct AttnArgs {
 };
 
 // Bounded wait on phase `parity` of `bar`. Gives up early when another role has aborted the CTA.
+// (Inline on purpose: a called function would need one register budget for roles that run under
+// different setmaxnreg limits.)
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
@@ -105,6 +107,18 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
     *abort = 1;
     return false;
 }
+
+// Position in the K/V stage ring: stage index and the parity of its current fill.
+struct Ring {
+    int s = 0;
+    uint32_t ph = 0;
+    __device__ __forceinline__ void next() {
+        if (++s == kStages) {
+            s = 0;
+            ph ^= 1u;
+        }
+    }
+};
 
 // Bounded wait used while shutting down: ignores the abort flag (outstanding copies and MMAs
 // must land before the CTA exits) but still gives up after the same limit.
@@ -219,10 +233,10 @@ __device__ __forceinline__ void producer(const CUtensorMap* mq, const CUtensorMa
         tc::tma_load_3d(dst + kHalfBytes, mq, kDim / 2, q0 + t * kRows, bh, &b->q_full[t]);
     }
     int it = 0;
-    for (; it < 2 * n; ++it) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
-        if (!wait_bar(&b->kv_empty[s], ph ^ 1u, abort)) break;
+    Ring r;
+    for (; it < 2 * n; ++it, r.next()) {
+        const int s = r.s;
+        if (!wait_bar(&b->kv_empty[s], r.ph ^ 1u, abort)) break;
         uint8_t* dst = smem + kOffKV + s * kTileBytes;
         const CUtensorMap* m = (it & 1) ? mv : mk;
         const int row = (it >> 1) * kKeys;
@@ -239,29 +253,44 @@ __device__ __forceinline__ void producer(const CUtensorMap* mq, const CUtensorMa
 
 __device__ __forceinline__ void mma_issuer(uint8_t* smem, Bars* b, uint32_t tmem, int n) {
     volatile int* abort = &b->abort;
-    const uint32_t q_addr = smem_u32(smem + kOffQ);
-    const uint32_t kv_addr = smem_u32(smem + kOffKV);
+    // Descriptors are built once; an operand step only adds its byte offset / 16 to the start-
+    // address field (bits 0-13, which cannot carry: shared addresses stay below 2^18 bytes).
+    const uint64_t q_desc = tc::sw128_desc(smem_u32(smem + kOffQ), 16, 1024);
+    const uint64_t k_desc = tc::sw128_desc(smem_u32(smem + kOffKV), 16, 1024);
+    const uint64_t v_desc = tc::sw128_desc(smem_u32(smem + kOffKV), kHalfBytes, 1024);
     // S_t = Q_t K^T: eight K=16 steps along the head dimension; 32 bytes per step inside a
     // 128-byte swizzled row, the second 64 columns in the other half tile.
     auto qk = [&](int t, int s) {
-        const uint32_t qa = q_addr + t * kTileBytes, ka = kv_addr + s * kTileBytes;
-#pragma unroll
-        for (int k = 0; k < kDim / 16; ++k) {
-            const uint32_t off = (k >> 2) * kHalfBytes + (k & 3) * 32;
-            tc::mma_ss(tmem + kColS0 + 128 * t, tc::sw128_desc(qa + off, 16, 1024), tc::sw128_desc(ka + off, 16, 1024),
-                       kIdescQK, k > 0);
-        }
+        const uint64_t qa = q_desc + ((t * kTileBytes) >> 4), ka = k_desc + ((s * kTileBytes) >> 4);
+        const uint32_t d = tmem + kColS0 + 128 * t;
+        constexpr uint32_t h = kHalfBytes >> 4;  // second 64 head columns
+        tc::mma_ss_at<0>(d, qa, ka, kIdescQK, 0u);
+        tc::mma_ss_at<2>(d, qa, ka, kIdescQK, 1u);
+        tc::mma_ss_at<4>(d, qa, ka, kIdescQK, 1u);
+        tc::mma_ss_at<6>(d, qa, ka, kIdescQK, 1u);
+        tc::mma_ss_at<h + 0>(d, qa, ka, kIdescQK, 1u);
+        tc::mma_ss_at<h + 2>(d, qa, ka, kIdescQK, 1u);
+        tc::mma_ss_at<h + 4>(d, qa, ka, kIdescQK, 1u);
+        tc::mma_ss_at<h + 6>(d, qa, ka, kIdescQK, 1u);
     };
     // O_t += P_t V: eight K=16 steps along the keys; P from TMEM (8 columns per step), V as an
     // MN-major operand (head dimension contiguous, 16 key rows = 2048 bytes per step, the second
     // 64 head columns 16 KB further).
     // Issued in two halves of 64 keys, each as soon as the softmax warps publish that half of P.
     auto pv = [&](int t, int s, int h, bool acc) {
-        const uint32_t va = kv_addr + s * kTileBytes;
-#pragma unroll
-        for (int k = 4 * h; k < 4 * h + 4; ++k)
-            tc::mma_ts(tmem + kColO0 + 128 * t, tmem + kColS0 + 128 * t + kColP + 8 * k,
-                       tc::sw128_desc(va + k * 2048, kHalfBytes, 1024), kIdescPV, (acc || k > 0) ? 1u : 0u);
+        const uint64_t va = v_desc + ((s * kTileBytes) >> 4);
+        const uint32_t d = tmem + kColO0 + 128 * t, pa = tmem + kColS0 + 128 * t + kColP;
+        if (h == 0) {
+            tc::mma_ts_at<0, 0>(d, pa, va, kIdescPV, acc ? 1u : 0u);
+            tc::mma_ts_at<8, 128>(d, pa, va, kIdescPV, 1u);
+            tc::mma_ts_at<16, 256>(d, pa, va, kIdescPV, 1u);
+            tc::mma_ts_at<24, 384>(d, pa, va, kIdescPV, 1u);
+        } else {
+            tc::mma_ts_at<32, 512>(d, pa, va, kIdescPV, 1u);
+            tc::mma_ts_at<40, 640>(d, pa, va, kIdescPV, 1u);
+            tc::mma_ts_at<48, 768>(d, pa, va, kIdescPV, 1u);
+            tc::mma_ts_at<56, 896>(d, pa, va, kIdescPV, 1u);
+        }
     };
     auto pv_tile = [&](int t, int s, bool acc, uint32_t parity) {
         for (int h = 0; h < 2; ++h) {
@@ -271,34 +300,41 @@ __device__ __forceinline__ void mma_issuer(uint8_t* smem, Bars* b, uint32_t tmem
         }
         return true;
     };
+    // kr: the next K tile's stage, vr: the next V tile's stage (tiles alternate K_0, V_0, K_1, ...).
+    Ring kr, vr;
+    vr.next();
     bool ok = wait_bar(&b->q_full[0], 0, abort) && wait_bar(&b->q_full[1], 0, abort) &&
-              wait_bar(&b->kv_full[0], 0, abort);
+              wait_bar(&b->kv_full[kr.s], kr.ph, abort);
     if (ok) {
         tc::fence_after();
-        qk(0, 0);
+        qk(0, kr.s);
         tc::commit(&b->s_full[0]);
-        qk(1, 0);
+        qk(1, kr.s);
         tc::commit(&b->s_full[1]);
-        tc::commit(&b->kv_empty[0]);
+        tc::commit(&b->kv_empty[kr.s]);
+        kr.next();
+        kr.next();
     }
     for (int j = 0; ok && j < n; ++j) {
-        const int itv = 2 * j + 1, sv = itv % kStages;
-        const int itk = 2 * j + 2, sk = itk % kStages;
         const bool more = j + 1 < n;
-        if (!(ok = wait_bar(&b->kv_full[sv], (itv / kStages) & 1u, abort))) break;
-        if (!(ok = pv_tile(0, sv, j > 0, j & 1u))) break;
+        if (!(ok = wait_bar(&b->kv_full[vr.s], vr.ph, abort))) break;
+        if (!(ok = pv_tile(0, vr.s, j > 0, j & 1u))) break;
         if (more) {
-            if (!(ok = wait_bar(&b->kv_full[sk], (itk / kStages) & 1u, abort))) break;
+            if (!(ok = wait_bar(&b->kv_full[kr.s], kr.ph, abort))) break;
             tc::fence_after();
-            qk(0, sk);
+            qk(0, kr.s);
             tc::commit(&b->s_full[0]);
         }
-        if (!(ok = pv_tile(1, sv, j > 0, j & 1u))) break;
-        tc::commit(&b->kv_empty[sv]);
+        if (!(ok = pv_tile(1, vr.s, j > 0, j & 1u))) break;
+        tc::commit(&b->kv_empty[vr.s]);
+        vr.next();
+        vr.next();
         if (more) {
-            qk(1, sk);
+            qk(1, kr.s);
             tc::commit(&b->s_full[1]);
-            tc::commit(&b->kv_empty[sk]);
+            tc::commit(&b->kv_empty[kr.s]);
+            kr.next();
+            kr.next();
         }
     }
     // Arrives when every MMA above has finished (at once if none was issued).

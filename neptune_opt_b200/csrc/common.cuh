@@ -25,6 +25,32 @@ int sm_count();
 void count_launch(int n = 1);
 int finish_launch(const char* what);  // checks cudaGetLastError, returns nb200_status
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// Kernels launched with launch_pdl may be scheduled while the previous kernel on the stream is
+// still draining, so the launch and CTA start-up overlap its tail. Each such kernel calls
+// pdl_wait() before its first global-memory access (read or write): it returns once the previous
+// kernel has completed and its writes are visible, so results are exactly those of plain stream
+// order. pdl_trigger() allows the next PDL kernel to be scheduled; it can start only after every
+// CTA of this grid has triggered or exited, so a grid never waits on a dependent for resources.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t st,
+                       Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 inline size_t dtype_size(int dtype) { return dtype == NB200_F32 ? 4 : 2; }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

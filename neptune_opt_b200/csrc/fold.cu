@@ -15,6 +15,8 @@ template <int S, typename T, int NV, bool VEC, bool CTA>
 __global__ void __launch_bounds__(CTA ? 512 : 256)
 fold_kernel(const T* __restrict__ x, T* __restrict__ out, int64_t rows, int64_t ncols,
             int64_t srow, int64_t scol, Params p) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[64];
     Group<CTA> grp{red, 0};
     const int G = CTA ? (int)blockDim.x : 32;
@@ -76,6 +78,8 @@ template <typename T, int NV, bool VEC, bool CTA>
 __global__ void __launch_bounds__(CTA ? 512 : 256)
 softmax_kernel(const T* __restrict__ x, T* __restrict__ y, T* __restrict__ lse, int64_t rows,
                int64_t ncols, int64_t srow, int64_t scol, int mode, int out_vec) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[64];
     Group<CTA> grp{red, 0};
     const int G = CTA ? (int)blockDim.x : 32;
@@ -120,6 +124,8 @@ template <typename T, int NV, bool VEC, bool CTA>
 __global__ void __launch_bounds__(CTA ? 512 : 256)
 l2norm_kernel(const T* __restrict__ x, T* __restrict__ y, T* __restrict__ norm, int64_t rows,
               int64_t ncols, int64_t srow, int64_t scol, int out_vec) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[64];
     Group<CTA> grp{red, 0};
     const int G = CTA ? (int)blockDim.x : 32;
@@ -161,6 +167,8 @@ template <int S, typename T, bool VEC>
 __global__ void __launch_bounds__(256)
 partial_kernel(const T* __restrict__ x, nb200_state* __restrict__ states, int64_t rows, int64_t cb,
                int64_t ns, int64_t srow, int64_t scol, int64_t cc, int64_t nparts, Params p) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[64];
     Group<true> grp{red, 0};
     const int G = (int)blockDim.x, t = (int)threadIdx.x;
@@ -200,6 +208,8 @@ template <int S, typename T>
 __global__ void __launch_bounds__(256)
 merge_kernel(const nb200_state* __restrict__ states, T* __restrict__ out, int64_t rows,
              int64_t nparts, int64_t rstride, int64_t pstride, Params p) {
+    pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t gid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int64_t ng = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -255,12 +265,12 @@ int fold_t(const T* x, T* out, int64_t rows, int64_t ncols, int64_t srow, int64_
     if (variant == NB200_VARIANT_WARP_ROW) {
         auto k = vec ? fold_kernel<S, T, 4, true, false> : fold_kernel<S, T, kScalarNV<T>, false, false>;
         const int g = persistent_grid(k, kWarpThreads, 0, (rows + 7) / 8, cps);
-        k<<<g, kWarpThreads, 0, st>>>(x, out, rows, ncols, srow, scol, p);
+        launch_pdl(k, g, kWarpThreads, 0, st, x, out, rows, ncols, srow, scol, p);
     } else {
         int threads = (L && L->threads) ? L->threads : (bytes >= 65536 ? 512 : 256);
         auto k = vec ? fold_kernel<S, T, 4, true, true> : fold_kernel<S, T, kScalarNV<T>, false, true>;
         const int g = persistent_grid(k, threads, 0, rows, cps);
-        k<<<g, threads, 0, st>>>(x, out, rows, ncols, srow, scol, p);
+        launch_pdl(k, g, threads, 0, st, x, out, rows, ncols, srow, scol, p);
     }
     count_launch();
     return finish_launch("nb200_fold");
@@ -345,7 +355,7 @@ int softmax_t(int mode, const T* x, T* y, T* lse, int64_t rows, int64_t ncols, i
               int64_t scol, const nb200_launch* L, cudaStream_t st) {
     const int out_vec = aligned16(y) && (ncols * (int64_t)sizeof(T)) % 16 == 0;
     return ReadoutPlan<T, SoftmaxK>::run(x, rows, ncols, srow, scol, L, st, [&](auto k, int g, int th) {
-        k<<<g, th, 0, st>>>(x, y, lse, rows, ncols, srow, scol, mode, out_vec);
+        launch_pdl(k, g, th, 0, st, x, y, lse, rows, ncols, srow, scol, mode, out_vec);
         count_launch();
         return finish_launch("nb200_softmax");
     });
@@ -356,7 +366,7 @@ int l2_t(const T* x, T* y, T* norm, int64_t rows, int64_t ncols, int64_t srow, i
          const nb200_launch* L, cudaStream_t st) {
     const int out_vec = aligned16(y) && (ncols * (int64_t)sizeof(T)) % 16 == 0;
     return ReadoutPlan<T, L2K>::run(x, rows, ncols, srow, scol, L, st, [&](auto k, int g, int th) {
-        k<<<g, th, 0, st>>>(x, y, norm, rows, ncols, srow, scol, out_vec);
+        launch_pdl(k, g, th, 0, st, x, y, norm, rows, ncols, srow, scol, out_vec);
         count_launch();
         return finish_launch("nb200_l2_normalize");
     });
@@ -369,7 +379,7 @@ int partial_t(const T* x, nb200_state* states, int64_t rows, int64_t cb, int64_t
     const bool vec = rows_vectorizable(x, rows, cb + ns, srow, scol) && cb % V == 0 && cc % V == 0;
     auto k = vec ? partial_kernel<S, T, true> : partial_kernel<S, T, false>;
     const int g = persistent_grid(k, 256, 0, rows * nparts, 0);
-    k<<<g, 256, 0, st>>>(x, states, rows, cb, ns, srow, scol, cc, nparts, p);
+    launch_pdl(k, g, 256, 0, st, x, states, rows, cb, ns, srow, scol, cc, nparts, p);
     count_launch();
     return finish_launch("nb200_fold_partial");
 }
@@ -379,7 +389,7 @@ int merge_t(const nb200_state* states, T* out, int64_t rows, int64_t nparts, int
             const Params& p, cudaStream_t st) {
     auto k = merge_kernel<S, T>;
     const int g = persistent_grid(k, 256, 0, (rows + 7) / 8, 0);
-    k<<<g, 256, 0, st>>>(states, out, rows, nparts, rs, ps, p);
+    launch_pdl(k, g, 256, 0, st, states, out, rows, nparts, rs, ps, p);
     count_launch();
     return finish_launch("nb200_fold_merge");
 }

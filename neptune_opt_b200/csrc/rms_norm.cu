@@ -15,6 +15,8 @@ template <typename T, int NV, bool VEC, bool CTA>
 __global__ void __launch_bounds__(CTA ? 512 : 256)
 rms_kernel(const T* __restrict__ x, const T* __restrict__ gamma, T* __restrict__ y, int64_t rows,
            int64_t ncols, int64_t srow, int64_t scol, int64_t sg, float eps, int gvec, int out_vec) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[64];
     Group<CTA> grp{red, 0};
     const int G = CTA ? (int)blockDim.x : 32;
@@ -91,7 +93,7 @@ int rms_t(const T* x, const T* gamma, T* y, int64_t rows, int64_t ncols, int64_t
                                           : (vecs <= 32 * 16 ? NB200_VARIANT_WARP_ROW : NB200_VARIANT_CTA_ROW);
     auto go = [&](auto k, int threads, int64_t work) {
         const int g = persistent_grid(k, threads, 0, work, cps);
-        k<<<g, threads, 0, st>>>(x, gamma, y, rows, ncols, srow, scol, sg, eps, gvec, out_vec);
+        launch_pdl(k, g, threads, 0, st, x, gamma, y, rows, ncols, srow, scol, sg, eps, gvec, out_vec);
         count_launch();
         return finish_launch("nb200_rms_norm");
     };

@@ -39,6 +39,8 @@ template <typename I>
 __global__ void __launch_bounds__(1024)
 spans_kernel(const I* __restrict__ seg, int64_t nseg, int64_t ss, int unsafe, int64_t nrows,
              int64_t* __restrict__ spans, uint32_t* __restrict__ status) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ int64_t warp_tot[32];
     __shared__ unsigned int st_s;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
@@ -134,6 +136,8 @@ __global__ void __launch_bounds__(256)
 pool16_kernel(const T* __restrict__ data, const I* __restrict__ bounds, int64_t bs, T* __restrict__ out,
               int64_t nrows, int64_t channels, int64_t srow, int64_t nseg, int reduce, int has_initial,
               uint32_t initial_bits, uint32_t* __restrict__ status) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int G = 32 / LPS, UNROLL = 8;
     const int lane = threadIdx.x & 31, sub = lane / LPS, sl = lane % LPS;
     const int64_t ntiles = (channels + 8 * LPS - 1) / (8 * LPS);
@@ -193,6 +197,8 @@ __global__ void __launch_bounds__(256)
 pool_kernel(const T* __restrict__ data, const I* __restrict__ bounds, int64_t bs, T* __restrict__ out,
             int64_t nrows, int64_t channels, int64_t srow, int64_t sch, int64_t nseg, int reduce, int has_initial,
             uint32_t initial_bits, uint32_t* __restrict__ status) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int CV = 4, UNROLL = 8;
     const int lane = threadIdx.x & 31;
     const int64_t gid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -250,7 +256,7 @@ int pool_t(const T* data, int64_t nrows, int64_t channels, int64_t srow, int64_t
                 const int64_t ntiles = (channels + 8 * lps - 1) / (8 * lps);
                 const int64_t per_warp = 32 / lps;
                 const int g = persistent_grid(k, 256, 0, (nseg * ntiles / per_warp + 8) / 8, 0);
-                k<<<g, 256, 0, st>>>(data, bounds, bs, out, nrows, channels, srow, nseg, reduce, has_initial, bits, status);
+                launch_pdl(k, g, 256, 0, st, data, bounds, bs, out, nrows, channels, srow, nseg, reduce, has_initial, bits, status);
                 count_launch();
                 return finish_launch("nb200_segment_pool");
             };
@@ -263,7 +269,7 @@ int pool_t(const T* data, int64_t nrows, int64_t channels, int64_t srow, int64_t
     auto k = pool_kernel<T, I>;
     const int64_t ntiles = (channels + 127) / 128;
     const int g = persistent_grid(k, 256, 0, (nseg * ntiles + 7) / 8, 0);
-    k<<<g, 256, 0, st>>>(data, bounds, bs, out, nrows, channels, srow, sch, nseg, reduce, has_initial, bits, status);
+    launch_pdl(k, g, 256, 0, st, data, bounds, bs, out, nrows, channels, srow, sch, nseg, reduce, has_initial, bits, status);
     count_launch();
     return finish_launch("nb200_segment_pool");
 }
@@ -284,9 +290,9 @@ int pool_idx(const T* data, int64_t nrows, int64_t channels, int64_t srow, int64
 int launch_spans(const void* seg, int idt, int64_t nseg, int64_t sstride, int unsafe, int64_t nrows,
                  int64_t* spans, uint32_t* status, cudaStream_t st) {
     if (idt == NB200_I32)
-        spans_kernel<int32_t><<<1, 1024, 0, st>>>((const int32_t*)seg, nseg, sstride, unsafe, nrows, spans, status);
+        launch_pdl(spans_kernel<int32_t>, 1, 1024, 0, st, (const int32_t*)seg, nseg, sstride, unsafe, nrows, spans, status);
     else
-        spans_kernel<int64_t><<<1, 1024, 0, st>>>((const int64_t*)seg, nseg, sstride, unsafe, nrows, spans, status);
+        launch_pdl(spans_kernel<int64_t>, 1, 1024, 0, st, (const int64_t*)seg, nseg, sstride, unsafe, nrows, spans, status);
     count_launch();
     return finish_launch("nb200_segment_spans");
 }

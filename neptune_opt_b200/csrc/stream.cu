@@ -15,7 +15,7 @@
 #include <algorithm>
 
 #include "launch.h"
-#include "stream.cuh"
+#include "row_ops.cuh"
 
 namespace nb200 {
 
@@ -26,223 +26,11 @@ struct RowPlan {
     int R, S, packed, warps;
 };
 
-// ------------------------------------------------------------------ packed arithmetic helpers
-__device__ __forceinline__ unsigned long long pk(float a, float b) {
-    return (static_cast<unsigned long long>(__float_as_uint(b)) << 32) | __float_as_uint(a);
-}
-__device__ __forceinline__ float lo_f(unsigned long long v) { return __uint_as_float(static_cast<uint32_t>(v)); }
-__device__ __forceinline__ float hi_f(unsigned long long v) { return __uint_as_float(static_cast<uint32_t>(v >> 32)); }
-__device__ __forceinline__ unsigned long long mul_f32x2(unsigned long long a, unsigned long long b) {
-    unsigned long long d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ unsigned long long add_f32x2(unsigned long long a, unsigned long long b) {
-    unsigned long long d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-
-// Two storage values of one 32-bit word as fp32 (low half first).
-template <typename T> struct Word;
-template <> struct Word<__nv_bfloat16> {
-    __device__ __forceinline__ static unsigned long long unpack(uint32_t w) {
-        return pk(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
-    }
-    // RN(a * g) of bf16 pairs: the product of two bf16 values is exact in fp32, so this is the
-    // reference's fp32 product rounded to bf16.
-    __device__ __forceinline__ static uint32_t round_pair(unsigned long long v) {
-        __nv_bfloat162 h = __floats2bfloat162_rn(lo_f(v), hi_f(v));
-        return *reinterpret_cast<uint32_t*>(&h);
-    }
-    __device__ __forceinline__ static uint32_t mul_pair(uint32_t a, uint32_t g) {
-        uint32_t d;
-        asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(g));
-        return d;
-    }
-};
-template <> struct Word<__half> {
-    __device__ __forceinline__ static unsigned long long unpack(uint32_t w) {
-        __half2 h = *reinterpret_cast<__half2*>(&w);
-        float2 f = __half22float2(h);
-        return pk(f.x, f.y);
-    }
-    __device__ __forceinline__ static uint32_t round_pair(unsigned long long v) {
-        __half2 h = __floats2half2_rn(lo_f(v), hi_f(v));
-        return *reinterpret_cast<uint32_t*>(&h);
-    }
-    __device__ __forceinline__ static uint32_t mul_pair(uint32_t a, uint32_t g) {
-        uint32_t d;
-        asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(g));
-        return d;
-    }
-};
-
-__device__ __forceinline__ uint32_t word(const uint4& u, int i) {
-    return i == 0 ? u.x : i == 1 ? u.y : i == 2 ? u.z : u.w;
-}
-
-// ------------------------------------------------------------------ Ops
-template <int S, typename T>
-struct FoldOp {
-    T* out;
-    Params p;
-    int nv;
-    __device__ __forceinline__ void prologue(unsigned char*) const {}
-    __device__ __forceinline__ void row(const uint4* v, int64_t r, int lane, const unsigned char*) const {
-        float res;
-        if constexpr (Sk<S>::kind == K_TWOPASS) {
-            constexpr int V = Elem<T>::V;
-            float sv[V], av[V];
-#pragma unroll
-            for (int e = 0; e < V; ++e) { sv[e] = 0.f; av[e] = 0.f; }
-            for (int j = lane; j < nv; j += 32) {
-                const uint4 u = v[j];
-#pragma unroll
-                for (int e = 0; e < V; ++e) sv[e] += Elem<T>::lane(u, e) * p.invN;
-            }
-            const float mean = warp_sum(combine_sum<V>(sv));
-            for (int j = lane; j < nv; j += 32) {
-                const uint4 u = v[j];
-#pragma unroll
-                for (int e = 0; e < V; ++e) {
-                    const float d = Elem<T>::lane(u, e) - mean;
-                    av[e] += p.invN * (d * d);
-                }
-            }
-            res = Sk<S>::fin(warp_sum(combine_sum<V>(av)));
-        } else {
-            res = finalize<S>(row_state<S, T>(v, nv, lane, p), p);
-        }
-        if (lane == 0) out[r] = Elem<T>::from_f(res);
-    }
-};
-
-template <typename T>
-struct SoftmaxOp {
-    T* y;
-    T* lse;
-    int64_t ncols;
-    int nv, mode;
-    __device__ __forceinline__ void prologue(unsigned char*) const {}
-    __device__ __forceinline__ void row(const uint4* v, int64_t r, int lane, const unsigned char*) const {
-        constexpr int V = Elem<T>::V;
-        const Params p{0.f, 0.f, 1.f, 1.f, 0.f, 0.f, 0.f};
-        const St s = row_state<NB200_LOGSUMEXP, T>(v, nv, lane, p);
-        const bool bad = s.status != 0 || !s.seen;
-        const float m = s.m, inv = 1.0f / s.acc, lg = logf(s.acc);
-        T* yrow = y + r * ncols;
-        for (int j = lane; j < nv; j += 32) {
-            const uint4 u = v[j];
-            float f[V];
-#pragma unroll
-            for (int e = 0; e < V; ++e) {
-                const float d = Elem<T>::lane(u, e) - m;
-                f[e] = bad ? NB200_NAN : (mode == 0 ? fexp(d) * inv : d - lg);
-            }
-            st_stream(yrow + (int64_t)j * V, Elem<T>::pack(f));
-        }
-        if (lse != nullptr && lane == 0) lse[r] = Elem<T>::from_f(finalize<NB200_LOGSUMEXP>(s, p));
-    }
-};
-
-template <typename T>
-struct L2Op {
-    T* y;
-    T* norm;
-    int64_t ncols;
-    int nv;
-    __device__ __forceinline__ void prologue(unsigned char*) const {}
-    __device__ __forceinline__ void row(const uint4* v, int64_t r, int lane, const unsigned char*) const {
-        constexpr int V = Elem<T>::V;
-        const Params p{0.f, 0.f, 1.f, 1.f, 0.f, 0.f, 0.f};
-        const float nrm = finalize<NB200_STABLE_L2>(row_state<NB200_STABLE_L2, T>(v, nv, lane, p), p);
-        const float inv = 1.0f / nrm;
-        T* yrow = y + r * ncols;
-        for (int j = lane; j < nv; j += 32) {
-            const uint4 u = v[j];
-            float f[V];
-#pragma unroll
-            for (int e = 0; e < V; ++e) f[e] = Elem<T>::lane(u, e) * inv;
-            st_stream(yrow + (int64_t)j * V, Elem<T>::pack(f));
-        }
-        if (norm != nullptr && lane == 0) norm[r] = Elem<T>::from_f(nrm);
-    }
-};
-
-// gamma (ncols values) is staged once per CTA at the start of shared memory.
-template <typename T>
-struct RmsOp {
-    T* y;
-    const T* gamma;
-    int64_t ncols, sg;
-    int nv;
-    float eps, count;
-    __device__ __forceinline__ void prologue(unsigned char* smem) const {
-        T* g = reinterpret_cast<T*>(smem);
-        for (int64_t c = threadIdx.x; c < ncols; c += blockDim.x) g[c] = gamma[c * sg];
-    }
-    __device__ __forceinline__ void row(const uint4* v, int64_t r, int lane, const unsigned char* smem) const {
-        constexpr int V = Elem<T>::V;
-        const uint4* g = reinterpret_cast<const uint4*>(smem);
-        T* yrow = y + r * ncols;
-        if constexpr (sizeof(T) == 2) {
-            // sum of squares: every square and every add rounded (no contraction), two lanes of
-            // fp32 per instruction
-            unsigned long long acc[4] = {0ull, 0ull, 0ull, 0ull};
-            for (int j = lane; j < nv; j += 32) {
-                const uint4 u = v[j];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const unsigned long long f = Word<T>::unpack(word(u, i));
-                    acc[i] = add_f32x2(acc[i], mul_f32x2(f, f));
-                }
-            }
-            const unsigned long long a01 = add_f32x2(acc[0], acc[1]), a23 = add_f32x2(acc[2], acc[3]);
-            const unsigned long long a = add_f32x2(a01, a23);
-            const float total = warp_sum(__fadd_rn(lo_f(a), hi_f(a)));
-            const float mean = __fdiv_rn(total, count);
-            const float scale = __frsqrt_rn(__fadd_rn(mean, eps));
-            const unsigned long long sc = pk(scale, scale);
-            for (int j = lane; j < nv; j += 32) {
-                const uint4 u = v[j], gg = g[j];
-                uint4 o;
-                o.x = Word<T>::mul_pair(Word<T>::round_pair(mul_f32x2(Word<T>::unpack(u.x), sc)), gg.x);
-                o.y = Word<T>::mul_pair(Word<T>::round_pair(mul_f32x2(Word<T>::unpack(u.y), sc)), gg.y);
-                o.z = Word<T>::mul_pair(Word<T>::round_pair(mul_f32x2(Word<T>::unpack(u.z), sc)), gg.z);
-                o.w = Word<T>::mul_pair(Word<T>::round_pair(mul_f32x2(Word<T>::unpack(u.w), sc)), gg.w);
-                st_stream(yrow + (int64_t)j * V, o);
-            }
-        } else {
-            unsigned long long acc0 = 0ull, acc1 = 0ull;
-            for (int j = lane; j < nv; j += 32) {
-                const uint4 u = v[j];
-                const unsigned long long a = pk(__uint_as_float(u.x), __uint_as_float(u.y));
-                const unsigned long long b = pk(__uint_as_float(u.z), __uint_as_float(u.w));
-                acc0 = add_f32x2(acc0, mul_f32x2(a, a));
-                acc1 = add_f32x2(acc1, mul_f32x2(b, b));
-            }
-            const unsigned long long acc = add_f32x2(acc0, acc1);
-            const float total = warp_sum(__fadd_rn(lo_f(acc), hi_f(acc)));
-            const float mean = __fdiv_rn(total, count);
-            const float scale = __frsqrt_rn(__fadd_rn(mean, eps));
-            const unsigned long long sc = pk(scale, scale);
-            for (int j = lane; j < nv; j += 32) {
-                const uint4 u = v[j], gg = g[j];
-                const unsigned long long a = mul_f32x2(mul_f32x2(pk(__uint_as_float(u.x), __uint_as_float(u.y)), sc),
-                                                       pk(__uint_as_float(gg.x), __uint_as_float(gg.y)));
-                const unsigned long long b = mul_f32x2(mul_f32x2(pk(__uint_as_float(u.z), __uint_as_float(u.w)), sc),
-                                                       pk(__uint_as_float(gg.z), __uint_as_float(gg.w)));
-                st_stream(yrow + (int64_t)j * V, make_uint4(static_cast<uint32_t>(a), static_cast<uint32_t>(a >> 32),
-                                                            static_cast<uint32_t>(b), static_cast<uint32_t>(b >> 32)));
-            }
-        }
-    }
-};
-
 // ------------------------------------------------------------------ resident-row kernel
 template <typename T, class Op>
 __global__ void __launch_bounds__(512) rows_kernel(const T* __restrict__ x, RowPlan pl, Op op) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(128) unsigned char smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + pl.bar_offset) + warp * pl.S;
@@ -284,7 +72,8 @@ __global__ void __launch_bounds__(512) rows_kernel(const T* __restrict__ x, RowP
         const int64_t r0 = b * pl.R;
         const int nr = (int)min((int64_t)pl.R, pl.rows - r0);
         for (int i = 0; i < nr; ++i)
-            op.row(reinterpret_cast<const uint4*>(stage + (size_t)i * pl.row_bytes), r0 + i, lane, smem);
+            op.row(SmemRow{reinterpret_cast<const uint4*>(stage + (size_t)i * pl.row_bytes), op.nv, lane}, r0 + i,
+                   lane, smem);
         __syncwarp();
         if (lane == 0 && b + pl.S * GW < pl.nblocks) {
             fence_proxy_async();
@@ -307,6 +96,8 @@ struct SpanPlan {
 template <int S_, typename T>
 __global__ void __launch_bounds__(512) span_kernel(const T* __restrict__ x, SpanPlan pl, Params p,
                                                    nb200_state* __restrict__ states, T* __restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int V = Elem<T>::V;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -377,8 +168,8 @@ __global__ void __launch_bounds__(512) span_kernel(const T* __restrict__ x, Span
         const int64_t c0 = cur.lo + (int64_t)cur.sub * pl.sub_cols;
         const int64_t c1 = max(c0, min(c0 + pl.sub_cols, cur.hi));
         const int nv = (int)((c1 - c0) / V);
-        const St sub = lane_state<S_, T>(reinterpret_cast<const uint4*>(ring + (size_t)stage_use * pl.stage_bytes), nv,
-                                         lane, p);
+        const St sub = lane_state<S_, T>(
+            SmemRow{reinterpret_cast<const uint4*>(ring + (size_t)stage_use * pl.stage_bytes), nv, lane}, p);
         run = merge_fast<S_>(run, sub, p);
         __syncwarp();
         if (lane == 0 && next.item < pl.nitems) {
@@ -468,7 +259,7 @@ int launch_rows(const T* x, const RowPlan& pl, const Op& op, cudaStream_t st, co
     if (rc) return rc;
     const int threads = pl.warps * 32;
     const int g = persistent_grid(k, threads, smem, (pl.nblocks + pl.warps - 1) / pl.warps, cps);
-    k<<<g, threads, smem, st>>>(x, pl, op);
+    launch_pdl(k, g, threads, smem, st, x, pl, op);
     count_launch();
     return finish_launch(what);
 }
@@ -488,6 +279,12 @@ int stream_fault_take(unsigned int* bits) {
 
 // Returns 1 (and launches) when the streaming path applies, 0 when the caller should use the
 // register-tiled kernels, negative on error.
+// The library's own policy (no launch given, or variant AUTO) sends 1-8 KB rows to the register-row
+// kernel; an explicit STREAM launch keeps the bulk-copy ring.
+template <typename T>
+inline bool use_ldg(const nb200_launch* L, int64_t ncols) {
+    return (!L || L->variant == NB200_VARIANT_AUTO) && ldg_rows_eligible((uint32_t)(ncols * (int64_t)sizeof(T)));
+}
 inline int plan_warps(const nb200_launch* L) { return (L && L->threads) ? L->threads / 32 : kStreamThreads / 32; }
 inline int plan_stages(const nb200_launch* L) { return L ? L->stages : 0; }
 inline int plan_cps(const nb200_launch* L) { return L ? L->ctas_per_sm : 0; }
@@ -496,10 +293,21 @@ template <typename T>
 int stream_fold_t(int sk, const Params& p, const T* x, int64_t rows, int64_t ncols, int64_t srow, int64_t scol,
                   T* out, const nb200_launch* L, cudaStream_t st) {
     if (!rows_streamable(x, rows, ncols, srow, scol)) return 0;
-    RowPlan pl;
-    if (!make_row_plan(rows, ncols, srow, sizeof(T), 0, pl, plan_warps(L), plan_stages(L))) return 0;
     const int nv = (int)(ncols / Elem<T>::V);
     int rc;
+    if (use_ldg<T>(L, ncols)) {
+        switch (sk) {
+#define X(S) case S: rc = launch_ldg_rows(x, rows, srow, FoldOp<S, T>{out, p, nv}, 0, st, "nb200_fold"); break;
+            X(NB200_LOGSUMEXP) X(NB200_LSE_BIASED) X(NB200_LSE_SCALED) X(NB200_SOFTCAP_LSE) X(NB200_STABLE_L2)
+            X(NB200_LINEAR_ATTN) X(NB200_DECAY_RENORM) X(NB200_SUMSQ_DIV) X(NB200_RMSNORM_MAX) X(NB200_VARIANCE)
+            X(NB200_STD)
+#undef X
+            default: return 0;
+        }
+        return rc ? rc : 1;
+    }
+    RowPlan pl;
+    if (!make_row_plan(rows, ncols, srow, sizeof(T), 0, pl, plan_warps(L), plan_stages(L))) return 0;
     switch (sk) {
 #define X(S) case S: rc = launch_rows(x, pl, FoldOp<S, T>{out, p, nv}, st, "nb200_fold", plan_cps(L)); break;
         X(NB200_LOGSUMEXP) X(NB200_LSE_BIASED) X(NB200_LSE_SCALED) X(NB200_SOFTCAP_LSE) X(NB200_STABLE_L2)
@@ -515,10 +323,14 @@ template <typename T>
 int stream_softmax_t(int mode, const T* x, int64_t rows, int64_t ncols, int64_t srow, int64_t scol, T* y, T* lse,
                      const nb200_launch* L, cudaStream_t st) {
     if (!rows_streamable(x, rows, ncols, srow, scol) || !aligned16(y)) return 0;
+    const SoftmaxOp<T> op{y, lse, ncols, (int)(ncols / Elem<T>::V), mode};
+    if (use_ldg<T>(L, ncols)) {
+        const int rc = launch_ldg_rows(x, rows, srow, op, 0, st, "nb200_softmax");
+        return rc ? rc : 1;
+    }
     RowPlan pl;
     if (!make_row_plan(rows, ncols, srow, sizeof(T), 0, pl, plan_warps(L), plan_stages(L))) return 0;
-    const int rc = launch_rows(x, pl, SoftmaxOp<T>{y, lse, ncols, (int)(ncols / Elem<T>::V), mode}, st, "nb200_softmax",
-                               plan_cps(L));
+    const int rc = launch_rows(x, pl, op, st, "nb200_softmax", plan_cps(L));
     return rc ? rc : 1;
 }
 
@@ -526,10 +338,14 @@ template <typename T>
 int stream_l2_t(const T* x, int64_t rows, int64_t ncols, int64_t srow, int64_t scol, T* y, T* norm,
                 const nb200_launch* L, cudaStream_t st) {
     if (!rows_streamable(x, rows, ncols, srow, scol) || !aligned16(y)) return 0;
+    const L2Op<T> op{y, norm, ncols, (int)(ncols / Elem<T>::V)};
+    if (use_ldg<T>(L, ncols)) {
+        const int rc = launch_ldg_rows(x, rows, srow, op, 0, st, "nb200_l2_normalize");
+        return rc ? rc : 1;
+    }
     RowPlan pl;
     if (!make_row_plan(rows, ncols, srow, sizeof(T), 0, pl, plan_warps(L), plan_stages(L))) return 0;
-    const int rc = launch_rows(x, pl, L2Op<T>{y, norm, ncols, (int)(ncols / Elem<T>::V)}, st, "nb200_l2_normalize",
-                               plan_cps(L));
+    const int rc = launch_rows(x, pl, op, st, "nb200_l2_normalize", plan_cps(L));
     return rc ? rc : 1;
 }
 
@@ -537,11 +353,17 @@ template <typename T>
 int stream_rms_t(const T* x, const T* gamma, int64_t rows, int64_t ncols, int64_t srow, int64_t scol, int64_t sg,
                  float eps, T* y, const nb200_launch* L, cudaStream_t st) {
     if (!rows_streamable(x, rows, ncols, srow, scol) || !aligned16(y)) return 0;
+    const RmsOp<T> op{y, gamma, ncols, sg, (int)(ncols / Elem<T>::V), eps, static_cast<float>(ncols)};
+    if (use_ldg<T>(L, ncols)) {
+        const uint32_t gbytes = (uint32_t)(ncols * (int64_t)sizeof(T));
+        int rc = gbytes > 48 * 1024 ? NB200_ERR_LAUNCH : NB200_OK;
+        if (!rc) rc = launch_ldg_rows(x, rows, srow, op, gbytes, st, "nb200_rms_norm");
+        return rc ? rc : 1;
+    }
     RowPlan pl;
     if (!make_row_plan(rows, ncols, srow, sizeof(T), (uint32_t)(ncols * (int64_t)sizeof(T)), pl, plan_warps(L),
                        plan_stages(L)))
         return 0;
-    const RmsOp<T> op{y, gamma, ncols, sg, (int)(ncols / Elem<T>::V), eps, static_cast<float>(ncols)};
     const int rc = launch_rows(x, pl, op, st, "nb200_rms_norm", plan_cps(L));
     return rc ? rc : 1;
 }
@@ -580,7 +402,7 @@ int stream_span_t(int sk, const Params& p, const T* x, int64_t rows, int64_t cb,
         rc = ensure_smem(k, smem);
         if (rc) return;
         const int g = persistent_grid(k, nw * 32, smem, (pl.nitems + nw - 1) / nw, L ? L->ctas_per_sm : 0);
-        k<<<g, nw * 32, smem, st>>>(x, pl, p, states, out);
+        launch_pdl(k, g, nw * 32, smem, st, x, pl, p, states, out);
         count_launch();
         rc = finish_launch(finalize ? "nb200_fold" : "nb200_fold_partial");
     };

@@ -104,10 +104,34 @@ __device__ __forceinline__ float combine_max(const float* a) {
     return s;
 }
 
-template <int S, typename T>
-__device__ __forceinline__ St lane_state(const uint4* v, int nv, int lane, const Params& p) {
+// ------------------------------------------------------------------ row sources
+// The vectors of a row one lane holds: 16-byte vector j (V elements) for j = lane, lane + 32, ...
+// below nv. for_each(f) calls f(u, j) for each of them in ascending j.
+struct SmemRow {  // staged in shared memory
+    const uint4* v;
+    int nv, lane;
+    template <class F>
+    __device__ __forceinline__ void for_each(F&& f) const {
+        for (int j = lane; j < nv; j += 32) f(v[j], j);
+    }
+};
+template <int NV>
+struct RegRow {  // held in registers, vector lane + 32 k in r[k] (a row of at most 32 NV vectors)
+    uint4 r[NV];
+    int nv, lane;
+    template <class F>
+    __device__ __forceinline__ void for_each(F&& f) const {
+#pragma unroll
+        for (int k = 0; k < NV; ++k)
+            if (lane + 32 * k < nv) f(r[k], lane + 32 * k);
+    }
+};
+
+template <int S, typename T, class Src>
+__device__ __forceinline__ St lane_state(const Src& src, const Params& p) {
     using K = Sk<S>;
     constexpr int V = Elem<T>::V;
+    const bool any = src.lane < src.nv;
     if constexpr (K::kind == K_LOG) {
         // Fast path: one max and one finiteness probe per element (phi * 0 is 0 for finite phi and
         // NaN for +-inf or NaN); when every element is finite the status is 0 and the max is the
@@ -115,15 +139,14 @@ __device__ __forceinline__ St lane_state(const uint4* v, int nv, int lane, const
         float mv[V], probe[V];
 #pragma unroll
         for (int e = 0; e < V; ++e) { mv[e] = -NB200_INF; probe[e] = 0.f; }
-        for (int j = lane; j < nv; j += 32) {
-            const uint4 u = v[j];
+        src.for_each([&](const uint4& u, int) {
 #pragma unroll
             for (int e = 0; e < V; ++e) {
                 const float ph = K::phi(Elem<T>::lane(u, e), p);
                 mv[e] = fmaxf(mv[e], ph);
                 probe[e] = fmaf(ph, 0.f, probe[e]);
             }
-        }
+        });
         const float mall = combine_max<V>(mv);
         if (combine_sum<V>(probe) == 0.f) {
             const bool seen = mall != -NB200_INF;
@@ -133,11 +156,10 @@ __device__ __forceinline__ St lane_state(const uint4* v, int nv, int lane, const
                 float av[V];
 #pragma unroll
                 for (int e = 0; e < V; ++e) av[e] = 0.f;
-                for (int j = lane; j < nv; j += 32) {
-                    const uint4 u = v[j];
+                src.for_each([&](const uint4& u, int) {
 #pragma unroll
                     for (int e = 0; e < V; ++e) av[e] += ex2(fmaf(K::phi(Elem<T>::lane(u, e), p), kLog2e, nm));
-                }
+                });
                 a = combine_sum<V>(av);
             }
             return St{mall, a, seen ? 1 : 0, 0};
@@ -145,8 +167,7 @@ __device__ __forceinline__ St lane_state(const uint4* v, int nv, int lane, const
         // A non-finite element is present: exact NaN / +inf status and the max over finite terms.
         float m = -NB200_INF;
         int st = 0;
-        for (int j = lane; j < nv; j += 32) {
-            const uint4 u = v[j];
+        src.for_each([&](const uint4& u, int) {
 #pragma unroll
             for (int e = 0; e < V; ++e) {
                 const float ph = K::phi(Elem<T>::lane(u, e), p);
@@ -154,53 +175,48 @@ __device__ __forceinline__ St lane_state(const uint4* v, int nv, int lane, const
                 else if (ph == NB200_INF) st |= 2;
                 else m = fmaxf(m, ph);
             }
-        }
+        });
         const bool seen = m != -NB200_INF;
         const float den = seen ? m : 0.f;
         float a = 0.f;
-        for (int j = lane; j < nv; j += 32) {
-            const uint4 u = v[j];
+        src.for_each([&](const uint4& u, int) {
 #pragma unroll
             for (int e = 0; e < V; ++e) {
                 const float ph = K::phi(Elem<T>::lane(u, e), p);
                 if (fabsf(ph) < NB200_INF) a += fexp(ph - den);
             }
-        }
+        });
         return St{m, a, seen ? 1 : 0, st};
     } else if constexpr (K::kind == K_MAXABS) {
         float mv[V], av[V];
 #pragma unroll
         for (int e = 0; e < V; ++e) { mv[e] = 0.f; av[e] = 0.f; }
-        for (int j = lane; j < nv; j += 32) {
-            const uint4 u = v[j];
+        src.for_each([&](const uint4& u, int) {
 #pragma unroll
             for (int e = 0; e < V; ++e) mv[e] = fmaxf(mv[e], fabsf(Elem<T>::lane(u, e)));
-        }
+        });
         const float m = combine_max<V>(mv);
         const float c = K::prep(K::floor ? fmaxf(m, 1e-30f) : m, p);
-        for (int j = lane; j < nv; j += 32) {
-            const uint4 u = v[j];
+        src.for_each([&](const uint4& u, int) {
 #pragma unroll
             for (int e = 0; e < V; ++e) av[e] += K::term_r(Elem<T>::lane(u, e), c);
-        }
-        return St{m, combine_sum<V>(av), lane < nv ? 1 : 0, 0};
+        });
+        return St{m, combine_sum<V>(av), any ? 1 : 0, 0};
     } else {  // K_SUMMAX
         float sv[V], av[V];
 #pragma unroll
         for (int e = 0; e < V; ++e) { sv[e] = 0.f; av[e] = -NB200_INF; }
-        for (int j = lane; j < nv; j += 32) {
-            const uint4 u = v[j];
+        src.for_each([&](const uint4& u, int) {
 #pragma unroll
             for (int e = 0; e < V; ++e) sv[e] += K::operand(Elem<T>::lane(u, e), p);
-        }
+        });
         const float m = combine_sum<V>(sv);
         const float r = K::term_scale(m, p);
-        for (int j = lane; j < nv; j += 32) {
-            const uint4 u = v[j];
+        src.for_each([&](const uint4& u, int) {
 #pragma unroll
             for (int e = 0; e < V; ++e) av[e] = fmaxf(av[e], Elem<T>::lane(u, e) * r);
-        }
-        return St{m, combine_max<V>(av), lane < nv ? 1 : 0, 0};
+        });
+        return St{m, combine_max<V>(av), any ? 1 : 0, 0};
     }
 }
 
@@ -244,23 +260,22 @@ __device__ __forceinline__ St warp_merge(St s, int lane, const Params& p) {
 // (emitters.py:459-488): the producer is reduced across the warp first, then every lane forms its
 // terms against the row's producer and the consumer is reduced across the warp. No repair is
 // needed inside a row, so this costs two warp reductions instead of a 32-state merge tree.
-template <int S, typename T>
-__device__ __forceinline__ St row_state(const uint4* v, int nv, int lane, const Params& p) {
+template <int S, typename T, class Src>
+__device__ __forceinline__ St row_state(const Src& src, const Params& p) {
     using K = Sk<S>;
     constexpr int V = Elem<T>::V;
     if constexpr (K::kind == K_LOG) {
         float mv[V], probe[V];
 #pragma unroll
         for (int e = 0; e < V; ++e) { mv[e] = -NB200_INF; probe[e] = 0.f; }
-        for (int j = lane; j < nv; j += 32) {
-            const uint4 u = v[j];
+        src.for_each([&](const uint4& u, int) {
 #pragma unroll
             for (int e = 0; e < V; ++e) {
                 const float ph = K::phi(Elem<T>::lane(u, e), p);
                 mv[e] = fmaxf(mv[e], ph);
                 probe[e] = fmaf(ph, 0.f, probe[e]);
             }
-        }
+        });
         const float mall = warp_max(combine_max<V>(mv));
         const bool finite = __all_sync(0xffffffffu, combine_sum<V>(probe) == 0.f);
         if (finite) {
@@ -270,51 +285,47 @@ __device__ __forceinline__ St row_state(const uint4* v, int nv, int lane, const 
             for (int e = 0; e < V; ++e) av[e] = 0.f;
             if (seen) {
                 const float nm = -mall * kLog2e;
-                for (int j = lane; j < nv; j += 32) {
-                    const uint4 u = v[j];
+                src.for_each([&](const uint4& u, int) {
 #pragma unroll
                     for (int e = 0; e < V; ++e) av[e] += ex2(fmaf(K::phi(Elem<T>::lane(u, e), p), kLog2e, nm));
-                }
+                });
             }
             return St{mall, warp_sum(combine_sum<V>(av)), seen ? 1 : 0, 0};
         }
         // a non-finite element: lane states with exact status, merged (rare path)
-        return warp_merge<S>(lane_state<S, T>(v, nv, lane, p), lane, p);
+        return warp_merge<S>(lane_state<S, T>(src, p), src.lane, p);
     } else if constexpr (K::kind == K_MAXABS) {
         float mv[V], av[V];
 #pragma unroll
         for (int e = 0; e < V; ++e) { mv[e] = 0.f; av[e] = 0.f; }
-        for (int j = lane; j < nv; j += 32) {
-            const uint4 u = v[j];
+        src.for_each([&](const uint4& u, int) {
 #pragma unroll
             for (int e = 0; e < V; ++e) mv[e] = fmaxf(mv[e], fabsf(Elem<T>::lane(u, e)));
-        }
+        });
         const float m = warp_max(combine_max<V>(mv));
         const float c = K::prep(K::floor ? fmaxf(m, 1e-30f) : m, p);
-        for (int j = lane; j < nv; j += 32) {
-            const uint4 u = v[j];
+        src.for_each([&](const uint4& u, int) {
 #pragma unroll
             for (int e = 0; e < V; ++e) av[e] += K::term_r(Elem<T>::lane(u, e), c);
-        }
+        });
         return St{m, warp_sum(combine_sum<V>(av)), 1, 0};
     } else {  // K_SUMMAX
         float sv[V], av[V];
 #pragma unroll
         for (int e = 0; e < V; ++e) { sv[e] = 0.f; av[e] = -NB200_INF; }
-        for (int j = lane; j < nv; j += 32) {
-            const uint4 u = v[j];
+        src.for_each([&](const uint4& u, int) {
 #pragma unroll
             for (int e = 0; e < V; ++e) sv[e] += K::operand(Elem<T>::lane(u, e), p);
-        }
+        });
         const float m = warp_sum(combine_sum<V>(sv));
         const float r = K::term_scale(m, p);
-        for (int j = lane; j < nv; j += 32) {
-            const uint4 u = v[j];
+        src.for_each([&](const uint4& u, int) {
 #pragma unroll
             for (int e = 0; e < V; ++e) av[e] = fmaxf(av[e], Elem<T>::lane(u, e) * r);
-        }
+        });
         return St{m, warp_max(combine_max<V>(av)), 1, 0};
     }
 }
+
 
 }  // namespace nb200

@@ -99,6 +99,34 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
         : "memory");
 }
 
+// The same two MMAs with compile-time operand offsets folded into the instruction sequence (the
+// descriptors' start-address fields advance by kOff 16-byte units; for mma_ts_at the A column
+// advances by kCol). Keeps the per-step descriptors out of the issuing thread's registers.
+template <uint32_t kOff>
+__device__ __forceinline__ void mma_ss_at(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "add.s64 da, %1, %5;\n\t"
+        "add.s64 db, %2, %5;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, {%6, %6, %6, %6}, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(kOff), "r"(0u)
+        : "memory");
+}
+template <uint32_t kCol, uint32_t kOff>
+__device__ __forceinline__ void mma_ts_at(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t.reg .b32 ta;\n\t.reg .b64 db;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "add.u32 ta, %1, %5;\n\t"
+        "add.s64 db, %2, %6;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [ta], db, %3, {%7, %7, %7, %7}, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "n"(kCol), "n"(kOff), "r"(0u)
+        : "memory");
+}
+
 // Instruction descriptor for kind::f16 with bf16 A and B and an fp32 accumulator: c_format F32
 // (bit 4), a_format/b_format BF16 (bits 7, 10), A K-major, B K-major or MN-major (bit 16),
 // N >> 3 at bit 17, M >> 4 at bit 24.
