@@ -231,6 +231,13 @@ template <typename T, class Op>
 int launch_ldg_rows(const T* x, int64_t rows, int64_t srow, const Op& op, uint32_t smem, cudaStream_t st,
                     const char* what);
 
+// Column-span folds (split-plan chunks, or whole rows with finalize = 1) with register sub-blocks
+// (rows_ldg.cu). Returns 1 when launched, 0 for a skeleton it does not take, negative on error.
+// Requires x, the span starts and the row stride 16-byte aligned.
+template <typename T>
+int launch_ldg_span(int sk, const Params& p, const T* x, int64_t rows, int64_t cb, int64_t ns, int64_t srow,
+                    int64_t cc, int64_t nparts, nb200_state* states, T* out, int finalize, cudaStream_t st);
+
 // Whether the register-row kernel takes a row of `row_bytes` (16-byte multiple) by default.
 inline bool ldg_rows_eligible(uint32_t row_bytes) { return row_bytes >= 1024 && row_bytes <= 8192; }
 

@@ -379,6 +379,8 @@ int stream_span_t(int sk, const Params& p, const T* x, int64_t rows, int64_t cb,
         cc % V)
         return 0;
     if (sk == NB200_VARIANCE || sk == NB200_STD) return 0;
+    if (!L || L->variant == NB200_VARIANT_AUTO) return launch_ldg_span<T>(sk, p, x, rows, cb, ns, srow, cc, nparts,
+                                                                          states, out, finalize, st);
     SpanPlan pl;
     pl.rows = rows;
     pl.srow = srow;

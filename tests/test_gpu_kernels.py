@@ -148,7 +148,7 @@ def test_split_plan_matches_oracle(block, oracle_mod):
         for shape in ((16, 70000), (3, 262144), (40, 5000)):
             if -(-shape[1] // block) > NB.MAX_SPLIT_PARTS:
                 continue
-            for dtype in ("float32", "bfloat16"):
+            for dtype in DTYPES:
                 x = (torch.randn(*shape, generator=gen) * 3).to(_t(dtype)).cuda()
                 out = NB.run(name, x, plan="split", block=block, **params)
                 ref = oracle_mod.fold(name, _oracle_rows(x), params)
