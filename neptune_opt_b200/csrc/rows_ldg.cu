@@ -85,7 +85,9 @@ __device__ __forceinline__ void load_block(RegRow<NV>& b, const uint4* base, int
 
 // 16-bit logsumexp sub-block: packed max with NaN propagation (a NaN or +inf in the block sends it
 // to the exact path), an online rescale of the lane's running sum when the block raises its max,
-// and 2^(x log2 e - m log2 e) with 3 of every 8 words on the FMA-pipe polynomial.
+// and 2^(x log2 e - m log2 e) on packed fp32 pairs. (Moving a share of the exponentials to an
+// FMA-pipe polynomial, as the attention kernel does, was measured slower here: this loop is
+// bound by instruction issue, not by the special-function unit.)
 template <typename T>
 __device__ __forceinline__ uint32_t max_nan2(uint32_t a, uint32_t b) {
     uint32_t d;
@@ -104,9 +106,6 @@ __device__ __forceinline__ uint64_t widen2(uint32_t w) {
         return f2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
     }
 }
-
-// Of every 8 words (16 elements), 3 take the polynomial exp2.
-constexpr bool poly_word(int i) { return (i & 7) == 1 || (i & 7) == 4 || (i & 7) == 6; }
 
 template <typename T>
 __device__ __forceinline__ void lse16_block(const RegRow<kSpanNV>& blk, St& run, const Params& p) {
@@ -140,12 +139,7 @@ __device__ __forceinline__ void lse16_block(const RegRow<kSpanNV>& blk, St& run,
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const uint64_t x = fma2(widen2<T>(w[i]), l2e, nm2);
-            uint64_t e;
-            if (poly_word(4 * k + i))
-                e = exp2_poly2(f2(fmaxf(f2lo(x), -126.f), fmaxf(f2hi(x), -126.f)));
-            else
-                e = f2(ex2_ftz(f2lo(x)), ex2_ftz(f2hi(x)));
-            acc[i & 1] = add2(acc[i & 1], e);
+            acc[i & 1] = add2(acc[i & 1], f2(ex2_ftz(f2lo(x)), ex2_ftz(f2hi(x))));
         }
     }
     const uint64_t a = add2(acc[0], acc[1]);
