@@ -329,6 +329,28 @@ def make_attention(torch, NB, seed, causal=False, batch=8):
                     f"{'causal' if causal else 'non-causal'} -> o bf16, lse fp32 (inputs {3 * b * h * s * d * 2 >> 20} MiB > L2)"}
 
 
+def make_sharded_split(torch, NB, seed, dist):
+    """BASELINE config 3b across GPUs: the columns of bf16 [512, 262144] split into one shard per
+    rank; each rank folds its shard into 16K-column chunk states, one NCCL all-gather moves the
+    states (16 B each), every rank merges them in ascending (rank, chunk) order. Total work is fixed
+    (strong scaling)."""
+    from neptune_opt_b200.parallel import sharded_split_fold
+
+    rows, ncols, block = 512, 262144, 16384
+    n = dist.world
+    width = ncols // n
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    xs = [(torch.randn(rows, width, device="cuda", generator=g) * 3.0).to(torch.bfloat16) for _ in range(2)]
+
+    def step(i):
+        sharded_split_fold("logsumexp", xs[i % 2], ncols, params={"tiny": 0.0}, chunk=block, widths=[width] * n)
+
+    return {"name": "wide_logsumexp_split_sharded", "step": step, "bytes": rows * ncols * 2 + rows * 2, "rows": rows,
+            "launches": 2, "buffers": 2,
+            "desc": f"logsumexp bf16 x[{rows},{ncols}] N(0,3^2), columns sharded over {n} GPUs ({width} each), "
+                    f"{block}-column chunk states all-gathered over NCCL and merged in rank order"}
+
+
 def gpu_id(torch) -> str:
     """nvidia-smi id of the current device (PCI bus id when torch exposes it)."""
     props = torch.cuda.get_device_properties(torch.cuda.current_device())
@@ -385,6 +407,52 @@ def tensor_roofline(flops_per_launch, ms, peaks, traffic):
     return {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
             "frac": round(achieved / peaks["bf16_tflops"], 4),
             "peak_source": peaks["source"] + " (burst cuBLAS bf16 GEMM)", "traffic": traffic}
+
+
+def time_collective_steps(torch, dist, step, steps, warmup):
+    """Max-over-ranks ms per step of a step that holds NCCL collectives.
+
+    Every rank runs the warm-up eagerly, then tries to capture the K steps into one CUDA graph
+    (capture records the collectives without running them). The ranks agree on the outcome with an
+    eager all-reduce before anything is replayed, so all of them either replay their graphs or all
+    time eager steps: the collectives stay matched on every path."""
+    import torch.distributed as td
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    g, ok = torch.cuda.CUDAGraph(), 1
+    try:
+        capture = torch.cuda.Stream()
+        capture.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.graph(g, stream=capture):
+            for i in range(steps):
+                step(warmup + i)
+    except Exception:  # noqa: BLE001 -- decided jointly below
+        ok = 0
+    torch.cuda.synchronize()
+    flag = torch.tensor([ok], dtype=torch.int32, device="cuda")
+    td.all_reduce(flag, op=td.ReduceOp.MIN)
+    graph = bool(flag.item())
+    if graph:
+        g.replay()  # untimed first replay
+        torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    if graph:
+        g.replay()
+    else:
+        for i in range(steps):
+            step(warmup + i)
+    end.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    del g
+    how = ("CUDA graph (partial, NCCL all-gather, merge captured together)" if graph
+           else "eager (graph capture was not possible on every rank)") + ", max over ranks"
+    return dist.max(start.elapsed_time(end) / steps), how
 
 
 def roofline(bytes_per_launch, ms, peaks, traffic):
@@ -549,6 +617,17 @@ def main():
                 "algorithmic_bytes_per_step": r["bytes"], "launches_per_step": r["launches"],
                 "traffic_bytes_per_launch": profile_traffic(r["name"]),
                 "l2_rotation_buffers": r["buffers"]}
+            del r
+            torch.cuda.empty_cache()
+        if n > 1:
+            r = make_sharded_split(torch, NB, 2600, dist)
+            steps = min(args.steps, 50)
+            sms_, how = time_collective_steps(torch, dist, r["step"], steps, max(3, args.warmup))
+            regions[r["name"]] = {
+                "workload": r["desc"], "ms_per_step": round(sms_, 5), "scaling": "strong",
+                "GB_per_s": round(r["bytes"] / (sms_ * 1e-3) / 1e9, 1),
+                "rows_per_s": round(r["rows"] / (sms_ * 1e-3), 1), "timing": how,
+                "algorithmic_bytes_per_step": r["bytes"]}
             del r
             torch.cuda.empty_cache()
         for causal in (False, True):

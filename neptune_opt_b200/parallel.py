@@ -123,7 +123,7 @@ def _cuda_merge(name, params, states, out):
 
 
 def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: int = 16384, group=None,
-                       partial_fn=None, merge_fn=None):
+                       partial_fn=None, merge_fn=None, widths=None):
     """Fold rows whose columns are sharded across the ranks of `group`, rank order = column order.
 
     Each rank passes its own [rows, width_r] block (the ranks' blocks concatenated along columns in
@@ -133,7 +133,9 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
 
     `partial_fn(name, params, x_shard, col_begin, ncols_total, chunk) -> int32 [rows, nparts, 4]` and
     `merge_fn(name, params, states, out)` default to the CUDA kernels; tests on CPU ranks substitute
-    their own to exercise the sharding and exchange logic.
+    their own to exercise the sharding and exchange logic. `widths` (every rank's shard width, in
+    rank order) skips the width exchange -- and its host synchronisation -- when the caller knows
+    the layout, as a steady-state loop does.
     """
     import torch
     import torch.distributed as td
@@ -147,10 +149,15 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
     world = td.get_world_size(group)
     rank = td.get_rank(group)
     rows, width = x_shard.shape
-    widths = torch.tensor([width], dtype=torch.int64, device=x_shard.device)
-    all_widths = [torch.zeros_like(widths) for _ in range(world)]
-    td.all_gather(all_widths, widths, group=group)
-    all_widths = [int(w.item()) for w in all_widths]
+    if widths is None:
+        mine = torch.tensor([width], dtype=torch.int64, device=x_shard.device)
+        gathered_w = [torch.zeros_like(mine) for _ in range(world)]
+        td.all_gather(gathered_w, mine, group=group)
+        all_widths = [int(w.item()) for w in gathered_w]
+    else:
+        all_widths = [int(w) for w in widths]
+        if len(all_widths) != world or all_widths[rank] != width:
+            raise ValueError(f"widths {all_widths} do not describe rank {rank}'s shard of width {width}")
     if sum(all_widths) != ncols_total:
         raise ValueError(f"column shards sum to {sum(all_widths)}, expected {ncols_total}")
     col_begin = sum(all_widths[:rank])

@@ -1,0 +1,95 @@
+"""Two-GPU NCCL run of the column-sharded split plan (the one multi-GPU path with an exchange).
+
+Each rank folds its column shard of a bf16 [64, 100000] block into chunk states, one NCCL
+all-gather exchanges them and every rank merges them in ascending (rank, chunk) order. The result
+must equal, bit for bit, the single-GPU merge of the same states in the same order, and match the
+oracle within 1 bf16 ulp. Runs as two spawned processes; skipped with fewer than two GPUs.
+"""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+
+from conftest import cuda_available
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_available(), reason="needs a CUDA device")]
+
+ROWS, NCOLS, CHUNK = 64, 100000, 8192
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, world, port, result_path):
+    import datetime
+
+    import torch
+    import torch.distributed as td
+
+    from neptune_opt_b200.parallel import shard_rows, sharded_split_fold
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    td.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                          device_id=torch.device("cuda", rank))
+    try:
+        gen = torch.Generator().manual_seed(21)
+        x = (torch.randn(ROWS, NCOLS, generator=gen) * 3).to(torch.bfloat16)
+        c0, c1 = shard_rows(NCOLS, world, rank)  # contiguous column block of this rank
+        shard = x[:, c0:c1].contiguous().cuda()
+        out = sharded_split_fold("logsumexp", shard, NCOLS, params={"tiny": 0.0}, chunk=CHUNK)
+        widths = [shard_rows(NCOLS, world, r)[1] - shard_rows(NCOLS, world, r)[0] for r in range(world)]
+        again = sharded_split_fold("logsumexp", shard, NCOLS, params={"tiny": 0.0}, chunk=CHUNK, widths=widths)
+        torch.cuda.synchronize()
+        if rank == 0:
+            torch.save({"out": out.cpu(), "again": again.cpu()}, result_path)
+        td.barrier()
+    finally:
+        td.destroy_process_group()
+
+
+def test_sharded_split_over_nccl_matches_single_gpu(tmp_path, oracle_mod):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    result = str(tmp_path / "r0.pt")
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, result)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    got = torch.load(result)
+
+    from conftest import assert_close_dtype
+    from neptune_opt_b200.parallel import _cuda_merge, _cuda_partial, shard_rows
+
+    gen = torch.Generator().manual_seed(21)
+    x = (torch.randn(ROWS, NCOLS, generator=gen) * 3).to(torch.bfloat16)
+    states = []
+    for r in range(2):  # the same shards and chunking on one GPU, states in (rank, chunk) order
+        c0, c1 = shard_rows(NCOLS, 2, r)
+        states.append(_cuda_partial("logsumexp", {"tiny": 0.0}, x[:, c0:c1].contiguous().cuda(), c0, NCOLS, CHUNK))
+    width = max(s.shape[1] for s in states)
+    for i, s in enumerate(states):
+        if s.shape[1] < width:
+            pad = torch.zeros(ROWS, width - s.shape[1], 4, dtype=s.dtype, device=s.device)
+            pad[..., 0] = torch.tensor(float("-inf")).view(torch.int32)
+            states[i] = torch.cat([s, pad], dim=1)
+    merged = _cuda_merge("logsumexp", {"tiny": 0.0}, torch.cat(states, dim=1).contiguous(),
+                         torch.empty(ROWS, dtype=torch.bfloat16, device="cuda"))
+    assert torch.equal(got["out"], merged.cpu()) and torch.equal(got["again"], merged.cpu())
+    ref = oracle_mod.fold("logsumexp", x.float().numpy(), {"tiny": 0.0})
+    assert_close_dtype(got["out"].float().numpy(), ref, "bfloat16")
