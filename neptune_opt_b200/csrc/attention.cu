@@ -133,15 +133,11 @@ __device__ __forceinline__ void drain_bar(uint64_t* bar, uint32_t parity) {
     atomicOr(&g_attn_fault, 2u);
 }
 
-// Of every 8 key pairs, kPolyPer8 take the polynomial path (spread evenly), the rest ex2.
-constexpr int kPolyPer8 = 3;
-constexpr bool poly_pair(int i) { return kPolyPer8 > 0 && ((i & 7) * kPolyPer8) % 8 < kPolyPer8; }
-
-// P for keys [64 h, 64 h + 64) of this row: p = 2^(s * sl2 - m) rounded to bf16 into TMEM
-// (one column per key pair, the lower key in the low half), fp32 p added to the row sums.
-// Masked tiles (some key past the row's last) use the special-function unit for every pair:
-// their -inf scores would need the polynomial's clamp anyway.
-template <bool kMasked>
+// P for keys [64 h, 64 h + 64) of this row: p = 2^(s * sl2 - m) on the special-function unit,
+// rounded to bf16 into TMEM (one column per key pair, the lower key in the low half), fp32 p added
+// to the row sums. (Computing a share of the exponentials with an FMA-pipe polynomial instead was
+// measured slower at every share tried, 2/8 to 5/8 of the pairs: the softmax warps run out of
+// issue slots before the special-function unit saturates.)
 __device__ __forceinline__ void p_half(const float* s, int h, uint64_t sl2, uint64_t nm, uint64_t& acc0,
                                        uint64_t& acc1, uint32_t tP) {
 #pragma unroll
@@ -151,11 +147,7 @@ __device__ __forceinline__ void p_half(const float* s, int h, uint64_t sl2, uint
         for (int i = 0; i < 16; ++i) {
             const int pi = 32 * h + 16 * c + i;
             const uint64_t x = fma2(f2(s[2 * pi], s[2 * pi + 1]), sl2, nm);
-            uint64_t p;
-            if (!kMasked && poly_pair(pi))
-                p = exp2_poly2(f2(fmaxf(f2lo(x), -126.f), fmaxf(f2hi(x), -126.f)));
-            else
-                p = f2(ex2_ftz(f2lo(x)), ex2_ftz(f2hi(x)));
+            const uint64_t p = f2(ex2_ftz(f2lo(x)), ex2_ftz(f2hi(x)));
             if (i & 1)
                 acc1 = add2(acc1, p);
             else
@@ -352,10 +344,7 @@ __device__ __forceinline__ void softmax_tile(const CUtensorMap* mo, uint8_t* sme
         uint64_t acc0 = 0, acc1 = 0;  // packed fp32 partial row sums (+0.0 bit patterns)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            if (masked)
-                p_half<true>(s, h, sl2x2, nm, acc0, acc1, tP);
-            else
-                p_half<false>(s, h, sl2x2, nm, acc0, acc1, tP);
+            p_half(s, h, sl2x2, nm, acc0, acc1, tP);
             tc::tmem_wait_st();
             tc::fence_before();
             __syncwarp();

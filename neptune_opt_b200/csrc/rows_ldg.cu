@@ -86,8 +86,8 @@ __device__ __forceinline__ void load_block(RegRow<NV>& b, const uint4* base, int
 // 16-bit logsumexp sub-block: packed max with NaN propagation (a NaN or +inf in the block sends it
 // to the exact path), an online rescale of the lane's running sum when the block raises its max,
 // and 2^(x log2 e - m log2 e) on packed fp32 pairs. (Moving a share of the exponentials to an
-// FMA-pipe polynomial, as the attention kernel does, was measured slower here: this loop is
-// bound by instruction issue, not by the special-function unit.)
+// FMA-pipe polynomial was measured slower here: this loop is bound by instruction issue, not by
+// the special-function unit.)
 template <typename T>
 __device__ __forceinline__ uint32_t max_nan2(uint32_t a, uint32_t b) {
     uint32_t d;
