@@ -21,7 +21,9 @@
 // only when every earlier MMA of the issuing thread has finished, so the arrival of S_t(j+1)
 // also means PV_t(j) is complete: the softmax warps may rescale O_t between reading S_t(j+1) and
 // publishing P_t(j+1) without a separate barrier. S_t(j+1) overwrites the columns PV_t(j) reads
-// P_t(j) from; the tensor pipe executes one thread's MMAs in issue order.
+// P_t(j) from; the tensor pipe executes one thread's MMAs in issue order. Under a causal mask
+// query tile 0 stops one key tile early: its rows end where tile 1's begin, so the unit's last key
+// tile lies entirely above tile 0's diagonal.
 //
 // Every wait is bounded (about a second of SM clock). A wait that runs out sets bit 1 of the
 // attention fault word and the CTA's abort flag; the other roles stop at their next wait, the
@@ -189,7 +191,9 @@ __device__ __forceinline__ void producer(const CUtensorMap* mq, const CUtensorMa
     for (int s = 0; s < kStages && s < it; ++s) drain_bar(&b->kv_full[s], ((it - 1 - s) / kStages) & 1u);
 }
 
-__device__ __forceinline__ void mma_issuer(uint8_t* smem, Bars* b, uint32_t tmem, int n) {
+// n K/V tiles in the unit; query tile 0 uses the first n0 of them (n0 = n, or n - 1 under a causal
+// mask, where tile 0's rows end 128 keys before tile 1's).
+__device__ __forceinline__ void mma_issuer(uint8_t* smem, Bars* b, uint32_t tmem, int n0, int n) {
     volatile int* abort = &b->abort;
     // Descriptors are built once; an operand step only adds its byte offset / 16 to the start-
     // address field (bits 0-13, which cannot carry: shared addresses stay below 2^18 bytes).
@@ -256,12 +260,14 @@ __device__ __forceinline__ void mma_issuer(uint8_t* smem, Bars* b, uint32_t tmem
     for (int j = 0; ok && j < n; ++j) {
         const bool more = j + 1 < n;
         if (!(ok = wait_bar(&b->kv_full[vr.s], vr.ph, abort))) break;
-        if (!(ok = pv_tile(0, vr.s, j > 0, j & 1u))) break;
+        if (j < n0 && !(ok = pv_tile(0, vr.s, j > 0, j & 1u))) break;
         if (more) {
             if (!(ok = wait_bar(&b->kv_full[kr.s], kr.ph, abort))) break;
             tc::fence_after();
-            qk(0, kr.s);
-            tc::commit(&b->s_full[0]);
+            if (j + 1 < n0) {
+                qk(0, kr.s);
+                tc::commit(&b->s_full[0]);
+            }
         }
         if (!(ok = pv_tile(1, vr.s, j > 0, j & 1u))) break;
         tc::commit(&b->kv_empty[vr.s]);
@@ -404,6 +410,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q0 = qb * kQTiles * kRows;
     const int kv_end = a.causal ? min(q0 + kQTiles * kRows, a.S) : a.S;
     const int n = (kv_end + kKeys - 1) / kKeys;
+    // Query tile 0 of a causal unit ends 128 rows earlier: its last K/V tile would be fully masked.
+    const int n0 = a.causal ? (min(q0 + kRows, a.S) + kKeys - 1) / kKeys : n;
 
     if (threadIdx.x == 0) {
         for (int t = 0; t < kQTiles; ++t) {
@@ -433,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // branch); both end at barrier 0, after which the MMA warp frees the tensor memory.
     if (warp < 8) {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
-        softmax_tile(&mo, smem, b, tmem, a, bh, q0, n);
+        softmax_tile(&mo, smem, b, tmem, a, bh, q0, warp < 4 ? n0 : n);
         tc::fence_before();
         asm volatile("bar.sync 0;" ::: "memory");
     } else {
@@ -442,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) producer(&mq, &mk, &mv, smem, b, bh, q0, n);
             __syncwarp();
         } else if (warp == kMmaWarp) {
-            if (lane == 0) mma_issuer(smem, b, tmem, n);
+            if (lane == 0) mma_issuer(smem, b, tmem, n0, n);
             __syncwarp();
         }
         tc::fence_before();
