@@ -63,6 +63,18 @@ static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsControl <= kThreads * kLaunchR
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS0 = 0, kColO0 = 256;  // tile t: S at kColS0 + 128 t, O at kColO0 + 128 t
 constexpr uint32_t kColP = 64;                // P inside S's columns
+// P is published in kPParts parts of 128 / kPParts keys; the MMA thread issues each part's P V
+// steps as soon as that part is in TMEM. Two parts measured fastest (interleaved A/B on one box,
+// non-causal: 2 parts 1059-1222, 4 parts 1001-1096, 8 parts 857-915 TFLOP/s): every further
+// hand-off (store wait, fence, arrival, one more wait in the MMA thread) costs more than the extra
+// overlap of the P V MMAs with the exponentials gains.
+#ifndef NB200_ATTN_PPARTS
+#define NB200_ATTN_PPARTS 2
+#endif
+constexpr int kPParts = NB200_ATTN_PPARTS;
+constexpr int kPairsPerPart = 64 / kPParts;  // TMEM columns of P per part (two keys per column)
+constexpr int kStepsPerPart = 8 / kPParts;   // K=16 P V MMA steps per part
+static_assert(kPParts == 2 || kPParts == 4 || kPParts == 8, "P parts");
 constexpr float kRescaleSlack = 8.f;          // keep a stale max while the new one is < 2^8 above it
 constexpr uint32_t kIdescQK = tc::idesc_bf16(128, 128, false);
 constexpr uint32_t kIdescPV = tc::idesc_bf16(128, 128, true);
@@ -77,7 +89,7 @@ struct Bars {
     uint64_t kv_full[kStages];
     uint64_t kv_empty[kStages];
     uint64_t s_full[kQTiles];
-    uint64_t p_full[kQTiles][2];  // per half of P (keys 0-63, 64-127)
+    uint64_t p_full[kQTiles][kPParts];  // per part of P (128 / kPParts keys each)
     uint64_t o_final;
     uint32_t tmem_base;
     int abort;
@@ -135,28 +147,34 @@ __device__ __forceinline__ void drain_bar(uint64_t* bar, uint32_t parity) {
     atomicOr(&g_attn_fault, 2u);
 }
 
-// P for keys [64 h, 64 h + 64) of this row: p = 2^(s * sl2 - m) on the special-function unit,
+// P for part qp of this row's keys: p = 2^(s * sl2 - m) on the special-function unit,
 // rounded to bf16 into TMEM (one column per key pair, the lower key in the low half), fp32 p added
 // to the row sums. (Computing a share of the exponentials with an FMA-pipe polynomial instead was
 // measured slower at every share tried, 2/8 to 5/8 of the pairs: the softmax warps run out of
 // issue slots before the special-function unit saturates.)
-__device__ __forceinline__ void p_half(const float* s, int h, uint64_t sl2, uint64_t nm, uint64_t& acc0,
+template <int kPairs = kPairsPerPart>
+__device__ __forceinline__ void p_part(const float* s, int qp, uint64_t sl2, uint64_t nm, uint64_t& acc0,
                                        uint64_t& acc1, uint32_t tP) {
+    uint32_t pk[kPairs];
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const int pi = 32 * h + 16 * c + i;
-            const uint64_t x = fma2(f2(s[2 * pi], s[2 * pi + 1]), sl2, nm);
-            const uint64_t p = f2(ex2_ftz(f2lo(x)), ex2_ftz(f2hi(x)));
-            if (i & 1)
-                acc1 = add2(acc1, p);
-            else
-                acc0 = add2(acc0, p);
-            pk[i] = tc::pack_bf16(f2lo(p), f2hi(p));
-        }
-        tc::tmem_st16(tP + 32 * h + 16 * c, pk);
+    for (int i = 0; i < kPairs; ++i) {
+        const int pi = kPairs * qp + i;
+        const uint64_t x = fma2(f2(s[2 * pi], s[2 * pi + 1]), sl2, nm);
+        const uint64_t p = f2(ex2_ftz(f2lo(x)), ex2_ftz(f2hi(x)));
+        if (i & 1)
+            acc1 = add2(acc1, p);
+        else
+            acc0 = add2(acc0, p);
+        pk[i] = tc::pack_bf16(f2lo(p), f2hi(p));
+    }
+    const uint32_t col = tP + kPairs * qp;
+    if constexpr (kPairs == 32) {
+        tc::tmem_st16(col, pk);
+        tc::tmem_st16(col + 16, pk + 16);
+    } else if constexpr (kPairs == 16) {
+        tc::tmem_st16(col, pk);
+    } else {
+        tc::tmem_st8(col, pk);
     }
 }
 
@@ -218,27 +236,32 @@ __device__ __forceinline__ void mma_issuer(uint8_t* smem, Bars* b, uint32_t tmem
     // O_t += P_t V: eight K=16 steps along the keys; P from TMEM (8 columns per step), V as an
     // MN-major operand (head dimension contiguous, 16 key rows = 2048 bytes per step, the second
     // 64 head columns 16 KB further).
-    // Issued in two halves of 64 keys, each as soon as the softmax warps publish that half of P.
-    auto pv = [&](int t, int s, int h, bool acc) {
-        const uint64_t va = v_desc + ((s * kTileBytes) >> 4);
-        const uint32_t d = tmem + kColO0 + 128 * t, pa = tmem + kColS0 + 128 * t + kColP;
-        if (h == 0) {
-            tc::mma_ts_at<0, 0>(d, pa, va, kIdescPV, acc ? 1u : 0u);
-            tc::mma_ts_at<8, 128>(d, pa, va, kIdescPV, 1u);
-            tc::mma_ts_at<16, 256>(d, pa, va, kIdescPV, 1u);
-            tc::mma_ts_at<24, 384>(d, pa, va, kIdescPV, 1u);
-        } else {
-            tc::mma_ts_at<32, 512>(d, pa, va, kIdescPV, 1u);
-            tc::mma_ts_at<40, 640>(d, pa, va, kIdescPV, 1u);
-            tc::mma_ts_at<48, 768>(d, pa, va, kIdescPV, 1u);
-            tc::mma_ts_at<56, 896>(d, pa, va, kIdescPV, 1u);
+    // One K=16 step k of O_t += P_t V (compile-time k after unrolling).
+    auto pv_step = [&](int k, uint32_t d, uint32_t pa, uint64_t va, uint32_t acc) {
+        switch (k) {
+            case 0: tc::mma_ts_at<0, 0>(d, pa, va, kIdescPV, acc); break;
+            case 1: tc::mma_ts_at<8, 128>(d, pa, va, kIdescPV, acc); break;
+            case 2: tc::mma_ts_at<16, 256>(d, pa, va, kIdescPV, acc); break;
+            case 3: tc::mma_ts_at<24, 384>(d, pa, va, kIdescPV, acc); break;
+            case 4: tc::mma_ts_at<32, 512>(d, pa, va, kIdescPV, acc); break;
+            case 5: tc::mma_ts_at<40, 640>(d, pa, va, kIdescPV, acc); break;
+            case 6: tc::mma_ts_at<48, 768>(d, pa, va, kIdescPV, acc); break;
+            default: tc::mma_ts_at<56, 896>(d, pa, va, kIdescPV, acc); break;
         }
     };
+    // Issued part by part, each as soon as the softmax warps publish that part of P.
     auto pv_tile = [&](int t, int s, bool acc, uint32_t parity) {
-        for (int h = 0; h < 2; ++h) {
-            if (!wait_bar(&b->p_full[t][h], parity, abort)) return false;
+        const uint64_t va = v_desc + ((s * kTileBytes) >> 4);
+        const uint32_t d = tmem + kColO0 + 128 * t, pa = tmem + kColS0 + 128 * t + kColP;
+#pragma unroll
+        for (int qp = 0; qp < kPParts; ++qp) {
+            if (!wait_bar(&b->p_full[t][qp], parity, abort)) return false;
             tc::fence_after();
-            pv(t, s, h, acc);
+#pragma unroll
+            for (int kk = 0; kk < kStepsPerPart; ++kk) {
+                const int k = qp * kStepsPerPart + kk;
+                pv_step(k, d, pa, va, (acc || k > 0) ? 1u : 0u);
+            }
         }
         return true;
     };
@@ -349,12 +372,12 @@ __device__ __forceinline__ void softmax_tile(const CUtensorMap* mo, uint8_t* sme
         const uint64_t sl2x2 = f2(sl2, sl2), nm = f2(-m, -m);
         uint64_t acc0 = 0, acc1 = 0;  // packed fp32 partial row sums (+0.0 bit patterns)
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            p_half(s, h, sl2x2, nm, acc0, acc1, tP);
+        for (int qp = 0; qp < kPParts; ++qp) {
+            p_part(s, qp, sl2x2, nm, acc0, acc1, tP);
             tc::tmem_wait_st();
             tc::fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&b->p_full[t][h]);
+            if (lane == 0) mbar_arrive(&b->p_full[t][qp]);
         }
         const uint64_t acc = add2(acc0, acc1);
         l += f2lo(acc) + f2hi(acc);
@@ -417,8 +440,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < kQTiles; ++t) {
             mbar_init(&b->q_full[t], 1);
             mbar_init(&b->s_full[t], 1);
-            mbar_init(&b->p_full[t][0], 4);  // one arrival per softmax warp
-            mbar_init(&b->p_full[t][1], 4);
+            for (int qp = 0; qp < kPParts; ++qp) mbar_init(&b->p_full[t][qp], 4);  // one arrival per softmax warp
         }
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&b->kv_full[s], 1);
