@@ -386,3 +386,51 @@ def test_streaming_kernels_never_timed_out():
 
     torch.cuda.synchronize()
     assert L.stream_fault() == 0
+
+
+def test_bulk_copy_paths_match_oracle(oracle_mod):
+    """The bulk-copy ring kernels: AUTO sends contiguous rows of 8-32 KB there (fold, softmax, L2,
+    RMSNorm), and an explicit STREAM launch forces them for 1-8 KB rows and for split-plan chunks."""
+    import torch
+
+    import neptune_opt_b200 as NB
+    import neptune_opt_b200._lib as L
+
+    lib = L.load()
+    gen = torch.Generator().manual_seed(17)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for dtype, ncols in (("float32", 4096), ("bfloat16", 12288), ("float16", 6000)):
+        x = (torch.randn(96, ncols, generator=gen) * 2).to(_t(dtype)).cuda()
+        rows = _oracle_rows(x)
+        for name in ("logsumexp", "stable_l2", "variance"):
+            params = {**NB.param_defaults(name), **TEST_PARAMS.get(name, {})}
+            ref = oracle_mod.fold(name, rows, params)
+            assert_close_dtype(NB.run(name, x, **params).float().cpu().numpy(), ref, dtype,
+                               atol32=1e-6 * (1 + _scale(ref)))
+        y, lse = NB.run_softmax_lse(x)
+        ry, rl = oracle_mod.softmax(rows)
+        assert_close_dtype(y.float().cpu().numpy(), ry, dtype)
+        assert_close_dtype(lse.float().cpu().numpy(), rl, dtype)
+        g = (1 + 0.1 * torch.randn(ncols, generator=gen)).to(_t(dtype)).cuda()
+        assert_rms_close(NB.run_rms_norm(x, g, eps=1e-6).float().cpu().numpy(),
+                         oracle_mod.rms_norm(rows, g.float().cpu().numpy(), 1e-6, dtype), dtype)
+
+    forced = L.launch_struct(L.VARIANT_STREAM, 0, 0, 0)
+    p = L.params_struct({"tiny": 0.0})
+    for dtype, shape in (("float32", (50, 2048)), ("bfloat16", (40, 1024))):
+        x = (torch.randn(*shape, generator=gen) * 3).to(_t(dtype)).cuda()
+        ref = oracle_mod.fold("logsumexp", _oracle_rows(x), {"tiny": 0.0})
+        out = torch.empty(shape[0], dtype=x.dtype, device="cuda")
+        L.check(lib.nb200_fold(0, ctypes.byref(p), ctypes.c_void_p(x.data_ptr()), DTYPES.index(dtype), shape[0],
+                               shape[1], shape[1], 1, ctypes.c_void_p(out.data_ptr()), ctypes.byref(forced), stream),
+                "stream fold")
+        assert_close_dtype(out.float().cpu().numpy(), ref, dtype, atol32=1e-6 * (1 + _scale(ref)))
+    x = (torch.randn(16, 70000, generator=gen) * 3).to(torch.bfloat16).cuda()
+    ref = oracle_mod.fold("logsumexp", _oracle_rows(x), {"tiny": 0.0})
+    nparts = -(-70000 // 8192)
+    scratch = torch.empty(int(lib.nb200_fold_split_scratch_bytes(16, nparts)), dtype=torch.uint8, device="cuda")
+    out = torch.empty(16, dtype=torch.bfloat16, device="cuda")
+    L.check(lib.nb200_fold_split(0, ctypes.byref(p), ctypes.c_void_p(x.data_ptr()), 1, 16, 70000, 70000, 1, 8192,
+                                 ctypes.c_void_p(scratch.data_ptr()), scratch.numel(), ctypes.c_void_p(out.data_ptr()),
+                                 ctypes.byref(forced), stream), "stream split")
+    assert_close_dtype(out.float().cpu().numpy(), ref, "bfloat16")
