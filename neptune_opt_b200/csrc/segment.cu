@@ -79,6 +79,115 @@ spans_kernel(const I* __restrict__ seg, int64_t nseg, int64_t ss, int unsafe, in
     if (tid == 0 && st_s && status) atomicOr(status, st_s);
 }
 
+// ------------------------------------------------------------------ spans, many CTAs
+// For long length vectors the single-CTA scan above would leave one SM streaming the whole vector.
+// Three launches split it without scratch memory or waits between CTAs: blocks of kSpanChunk
+// lengths each own spans[b*kSpanChunk + 1 .. (b+1)*kSpanChunk], and the first slot of that range
+// carries the block's sum (K1), then its exclusive offset (K2), before K3 -- which reads only its
+// own slot -- overwrites the range with the final boundaries. Status bits as spans_kernel.
+constexpr int kSpanChunkThreads = 256;
+constexpr int kSpanPerThread = 16;
+constexpr int64_t kSpanChunk = (int64_t)kSpanChunkThreads * kSpanPerThread;
+
+__device__ __forceinline__ int64_t block_excl_scan(int64_t v, int64_t* warp_tot, int64_t& total) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int64_t incl = warp_incl_scan(v);
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    int64_t before = 0;
+    total = 0;
+    for (int w = 0; w < nw; ++w) {
+        if (w < warp) before += warp_tot[w];
+        total += warp_tot[w];
+    }
+    __syncthreads();
+    return before + incl - v;
+}
+
+template <typename I>
+__global__ void __launch_bounds__(kSpanChunkThreads)
+spans_sum_kernel(const I* __restrict__ seg, int64_t nseg, int64_t ss, int64_t nrows, int64_t* __restrict__ spans,
+                 uint32_t* __restrict__ status) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ int64_t warp_tot[32];
+    const int64_t b0 = (int64_t)blockIdx.x * kSpanChunk;
+    const int64_t lo = b0 + (int64_t)threadIdx.x * kSpanPerThread, hi = min(lo + kSpanPerThread, nseg);
+    unsigned int st = 0u;
+    int64_t local = 0;
+    for (int64_t i = lo; i < hi; ++i) {
+        const int64_t v = (int64_t)seg[i * ss];
+        if (v < 0 || v > nrows) st |= 1u;
+        if (v < 0) st |= 8u;
+        local += v;
+    }
+    int64_t total;
+    block_excl_scan(local, warp_tot, total);
+    if (threadIdx.x == 0) spans[b0 + 1] = total;
+    st = __reduce_or_sync(0xffffffffu, st);
+    if ((threadIdx.x & 31) == 0 && st && status) atomicOr(status, st);
+}
+
+__global__ void __launch_bounds__(1024)
+spans_offsets_kernel(int64_t nseg, int64_t nblocks, int unsafe, int64_t nrows, int64_t* __restrict__ spans,
+                     uint32_t* __restrict__ status) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ int64_t warp_tot[32];
+    const int64_t per = (nblocks + blockDim.x - 1) / blockDim.x;
+    const int64_t lo = min((int64_t)threadIdx.x * per, nblocks), hi = min(lo + per, nblocks);
+    int64_t local = 0;
+    for (int64_t b = lo; b < hi; ++b) local += spans[b * kSpanChunk + 1];
+    int64_t total;
+    int64_t run = block_excl_scan(local, warp_tot, total);
+    for (int64_t b = lo; b < hi; ++b) {
+        const int64_t sum = spans[b * kSpanChunk + 1];
+        spans[b * kSpanChunk + 1] = run;
+        run += sum;
+    }
+    if (threadIdx.x == 0) {
+        spans[0] = 0;
+        unsigned int st = 0u;
+        if (total < 0 || total > nrows) st |= 4u;
+        if (!unsafe && total != nrows) st |= 2u;
+        if (st && status) atomicOr(status, st);
+    }
+}
+
+template <typename I>
+__global__ void __launch_bounds__(kSpanChunkThreads)
+spans_write_kernel(const I* __restrict__ seg, int64_t nseg, int64_t ss, int64_t nrows, int64_t* __restrict__ spans,
+                   uint32_t* __restrict__ status) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ int64_t warp_tot[32];
+    __shared__ int64_t offset;
+    const int64_t b0 = (int64_t)blockIdx.x * kSpanChunk;
+    if (threadIdx.x == 0) offset = spans[b0 + 1];
+    const int64_t lo = b0 + (int64_t)threadIdx.x * kSpanPerThread, hi = min(lo + kSpanPerThread, nseg);
+    int64_t v[kSpanPerThread];
+    int64_t local = 0;
+#pragma unroll
+    for (int k = 0; k < kSpanPerThread; ++k) {
+        v[k] = lo + k < hi ? (int64_t)seg[(lo + k) * ss] : 0;
+        local += v[k];
+    }
+    int64_t total;
+    int64_t run = block_excl_scan(local, warp_tot, total);  // its barriers also publish `offset`
+    run += offset;
+    unsigned int st = 0u;
+#pragma unroll
+    for (int k = 0; k < kSpanPerThread; ++k) {
+        if (lo + k < hi) {
+            run += v[k];
+            spans[lo + k + 1] = run;
+            if (run < 0 || run > nrows) st |= 4u;
+        }
+    }
+    st = __reduce_or_sync(0xffffffffu, st);
+    if ((threadIdx.x & 31) == 0 && st && status) atomicOr(status, st);
+}
+
 // ------------------------------------------------------------------ pooling
 template <typename T> struct Pack;
 template <> struct Pack<__half> {
@@ -289,6 +398,24 @@ int pool_idx(const T* data, int64_t nrows, int64_t channels, int64_t srow, int64
 
 int launch_spans(const void* seg, int idt, int64_t nseg, int64_t sstride, int unsafe, int64_t nrows,
                  int64_t* spans, uint32_t* status, cudaStream_t st) {
+    if (nseg > 4 * kSpanChunk) {  // long vectors: three launches over many CTAs
+        const int64_t nb = (nseg + kSpanChunk - 1) / kSpanChunk;
+        if (idt == NB200_I32)
+            launch_pdl(spans_sum_kernel<int32_t>, (unsigned)nb, kSpanChunkThreads, 0, st, (const int32_t*)seg, nseg,
+                       sstride, nrows, spans, status);
+        else
+            launch_pdl(spans_sum_kernel<int64_t>, (unsigned)nb, kSpanChunkThreads, 0, st, (const int64_t*)seg, nseg,
+                       sstride, nrows, spans, status);
+        launch_pdl(spans_offsets_kernel, 1, 1024, 0, st, nseg, nb, unsafe, nrows, spans, status);
+        if (idt == NB200_I32)
+            launch_pdl(spans_write_kernel<int32_t>, (unsigned)nb, kSpanChunkThreads, 0, st, (const int32_t*)seg, nseg,
+                       sstride, nrows, spans, status);
+        else
+            launch_pdl(spans_write_kernel<int64_t>, (unsigned)nb, kSpanChunkThreads, 0, st, (const int64_t*)seg, nseg,
+                       sstride, nrows, spans, status);
+        count_launch(3);
+        return finish_launch("nb200_segment_spans");
+    }
     if (idt == NB200_I32)
         launch_pdl(spans_kernel<int32_t>, 1, 1024, 0, st, (const int32_t*)seg, nseg, sstride, unsafe, nrows, spans, status);
     else

@@ -434,3 +434,50 @@ def test_bulk_copy_paths_match_oracle(oracle_mod):
                                  ctypes.c_void_p(scratch.data_ptr()), scratch.numel(), ctypes.c_void_p(out.data_ptr()),
                                  ctypes.byref(forced), stream), "stream split")
     assert_close_dtype(out.float().cpu().numpy(), ref, "bfloat16")
+
+
+def test_long_length_vectors_build_spans_bit_exactly(oracle_mod):
+    """Length vectors past 16384 segments take the three-launch, many-CTA span construction: the
+    spans and the status bits must equal the oracle's for valid vectors, strided int32 views, and
+    violations placed in interior blocks (negative length, oversized length, lengths that do not
+    cover the rows with and without `unsafe`)."""
+    import torch
+
+    import neptune_opt_b200._lib as L
+
+    lib = L.load()
+    gen = torch.Generator().manual_seed(23)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def run(lengths, nrows, unsafe, idt):
+        n = lengths.shape[0]
+        spans = torch.full((n + 1,), -7, dtype=torch.int64, device="cuda")
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        L.check(lib.nb200_segment_spans(ctypes.c_void_p(lengths.data_ptr()), idt, n, lengths.stride(0), int(unsafe),
+                                        nrows, ctypes.c_void_p(spans.data_ptr()), ctypes.c_void_p(status.data_ptr()),
+                                        stream), "spans")
+        torch.cuda.synchronize()
+        return spans.cpu().numpy(), int(status.item())
+
+    for nseg in (16385, 100000, 200000, 4096 * 37 + 1):
+        lengths = torch.poisson(torch.full((nseg,), 20.0), generator=gen).clamp(1, 200).to(torch.int64)
+        T = int(lengths.sum())
+        cases = [("valid", lengths.clone(), T, False)]
+        bad = lengths.clone()
+        bad[nseg // 2] = -3
+        cases.append(("negative", bad, T, False))
+        big = lengths.clone()
+        big[nseg - 5] = T + 10
+        cases.append(("oversized", big, T, False))
+        cases.append(("short cover", lengths.clone(), T + 5, False))
+        cases.append(("short cover, unsafe", lengths.clone(), T + 5, True))
+        for label, lens, nrows, unsafe in cases:
+            want, wst = oracle_mod.segment_spans(lens.numpy(), False, unsafe, nrows)
+            got, gst = run(lens.cuda(), nrows, unsafe, L.INDEX_CODES["int64"])
+            assert np.array_equal(got, want) and gst == wst, f"{nseg} {label}: status {gst} vs {wst}"
+        wide = torch.zeros(nseg, 2, dtype=torch.int32)
+        wide[:, 0] = lengths.to(torch.int32)
+        view = wide.cuda()[:, 0]  # int32, element stride 2
+        want, wst = oracle_mod.segment_spans(lengths.numpy(), False, False, T)
+        got, gst = run(view, T, False, L.INDEX_CODES["int32"])
+        assert np.array_equal(got, want) and gst == wst, f"{nseg} strided int32"
