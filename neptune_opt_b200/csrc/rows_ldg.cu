@@ -22,11 +22,15 @@ constexpr int kLdgThreads = 128;
 // the finer 4-warp CTAs (softmax fp32 [8192, 2048]: 26.7 vs 27.6 us).
 template <class Op> struct LdgThreads { static constexpr int value = kLdgThreads; };
 template <typename T> struct LdgThreads<RmsOp<T>> { static constexpr int value = 256; };
-// The softmax readout is held to 5 CTAs per SM worth of registers (at most 102 per thread): 20
-// resident rows per SM instead of 16 (fp32 [8192, 2048]: 23.7 vs 26.6 us, no spills). The other ops
-// keep the compiler's choice (the same cap spills for some fold skeletons).
+// The softmax readout and the folds are held to 5 CTAs per SM worth of registers (at most 102 per
+// thread): 20 resident rows per SM instead of 16 (fp32 [8192, 2048]: softmax 23.7 vs 26.6 us,
+// logsumexp 14.4 vs 15.8 us, no spills). softcap_lse and variance would spill under the cap and
+// keep the compiler's choice, as do L2 and RMSNorm.
 template <class Op> struct LdgMinBlocks { static constexpr int value = 1; };
 template <typename T> struct LdgMinBlocks<SoftmaxOp<T>> { static constexpr int value = 5; };
+template <int S, typename T> struct LdgMinBlocks<FoldOp<S, T>> {
+    static constexpr int value = (S == NB200_SOFTCAP_LSE || S == NB200_VARIANCE) ? 1 : 5;
+};
 
 template <typename T, class Op, int NV, int kThreads = LdgThreads<Op>::value>
 __global__ void __launch_bounds__(kThreads, LdgMinBlocks<Op>::value)
