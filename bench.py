@@ -582,22 +582,20 @@ def main():
     xh = torch.randn(rows, ncols, dtype=torch.bfloat16).pin_memory()
     gh = (1 + 0.1 * torch.randn(ncols)).to(torch.bfloat16).pin_memory()
     oh = torch.empty(rows, ncols, dtype=torch.bfloat16).pin_memory()
-    xd = torch.empty(rows, ncols, dtype=torch.bfloat16, device="cuda")
-    gd = torch.empty(ncols, dtype=torch.bfloat16, device="cuda")
 
     def e2e_step(_i):
-        xd.copy_(xh, non_blocking=True)
-        gd.copy_(gh, non_blocking=True)
-        out = NB.run_rms_norm(xd, gd, eps=1e-6)
-        oh.copy_(out, non_blocking=True)
+        # Rows stream through the GPU in 16 MiB chunks; the copies in and out of the device
+        # overlap each other and the kernel (nb200_rms_norm_host).
+        NB.run_rms_norm_host(xh, gh, eps=1e-6, out=oh)
 
     e2e_steps = max(3, min(args.steps, 30))
     e2e_ms, _ = time_steps(torch, dist, e2e_step, e2e_steps, 3, graph=False)
     e2e = {"value": round(n * w["bytes"] / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
            "h2d_bytes_per_step": rows * ncols * 2 + ncols * 2, "d2h_bytes_per_step": rows * ncols * 2,
            "ms_per_step": round(e2e_ms, 4), "steps": e2e_steps,
-           "path": "pinned host x,gamma -> H2D -> neptune_opt_b200.run_rms_norm -> D2H into pinned host"}
-    del xh, gh, oh, xd, gd
+           "path": "pinned host x,gamma -> neptune_opt_b200.run_rms_norm_host (nb200_rms_norm_host: 16 MiB "
+                   "row chunks, H2D / kernel / D2H overlapped on three streams) -> pinned host y"}
+    del xh, gh, oh
 
     # ---- the other fused regions
     regions = {}

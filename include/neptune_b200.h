@@ -183,6 +183,20 @@ int nb200_rms_norm(const void* x, const void* gamma, int dtype, int64_t rows, in
                    int64_t stride_row, int64_t stride_col, int64_t stride_gamma,
                    double eps, void* out, const nb200_launch* launch, void* stream);
 
+/* RMSNorm over rows held in HOST memory (no counterpart in the reference, whose ops take device
+ * tensors): x[rows, ncols] and gamma[ncols] contiguous host buffers (page-locked for the copies to
+ * overlap), y[rows, ncols] a host buffer. Rows move through the device in chunks of chunk_rows
+ * (0: about 16 MiB per chunk): while chunk k runs on `stream`, chunk k+1 is copied in and chunk
+ * k-1 copied back on two helper streams, so both PCIe directions are busy at once. The rows of y
+ * equal nb200_rms_norm's on the same rows. work: device memory, 256-byte aligned, of
+ * nb200_rms_norm_host_work_bytes(dtype, ncols, chunk_rows) bytes (gamma plus two input and two
+ * output chunks). The copies wait for earlier work on `stream`, and `stream` waits for the last
+ * copy back: y is complete once `stream` is. Calls on one device serialise their enqueueing. */
+int64_t nb200_rms_norm_host_work_bytes(int dtype, int64_t ncols, int64_t chunk_rows);
+int nb200_rms_norm_host(const void* x, const void* gamma, int dtype, int64_t rows, int64_t ncols,
+                        double eps, void* y, int64_t chunk_rows, void* work, int64_t work_bytes,
+                        void* stream);
+
 /* ------------------------------------------------------------------ a4/a5: segments
  * Descriptor status bits, ORed into a caller-owned device word (never a device assert):
  * 1 a length is negative or > nrows, 2 lengths do not cover nrows (checked unless unsafe),

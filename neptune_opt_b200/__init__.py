@@ -20,8 +20,8 @@ from neptune_opt_b200.attention import attention_op, run_attention  # noqa: F401
 from neptune_opt_b200.skeletons import (SKELETONS, all_registered, op_parameters, param_defaults,  # noqa: F401
                                         supported)
 from neptune_opt_b200.template import (MAX_SPLIT_PARTS, launch_reduction, run, run_l2_normalize,  # noqa: F401
-                                       run_rms_norm, run_softmax, run_softmax_lse, split_launch_shape,
-                                       validate_plan, validate_rms_inputs)
+                                       run_rms_norm, run_rms_norm_host, run_softmax, run_softmax_lse,
+                                       split_launch_shape, validate_plan, validate_rms_inputs)
 from neptune_opt_b200.torch_op import (_CUDA_OPS, _TRITON_OPS, as_cuda_op, as_segment_op,  # noqa: F401
                                        as_state_op, as_triton_op, check_segment_status, cuda_op_name,
                                        op_handle, run_segment_pool, segment_op_handle, softmax_op_handle,
@@ -85,7 +85,7 @@ __all__ = [
     "attention", "attention_op", "run_attention",
     "as_state_op", "as_triton_op", "autotune", "check_segment_status", "cuda_op_name", "l2_normalize",
     "launch_count", "log_softmax", "op_handle", "op_parameters", "param_defaults", "rms_norm", "run",
-    "run_l2_normalize", "run_rms_norm", "run_segment_pool", "run_softmax", "run_softmax_lse",
+    "run_l2_normalize", "run_rms_norm", "run_rms_norm_host", "run_segment_pool", "run_softmax", "run_softmax_lse",
     "segment_mean", "segment_op_handle", "segment_status", "segment_sum", "softmax", "softmax_op_handle",
     "split_launch_shape", "state_op_handle", "supported", "triton_op_name", "validate_rms_inputs",
     "validate_segment_inputs",

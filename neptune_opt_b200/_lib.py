@@ -64,6 +64,8 @@ SIGNATURES = {
     "nb200_fold_merge": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
     "nb200_rms_norm": (_int, [_vp, _vp, _int, _i64, _i64, _i64, _i64, _i64, _dbl, _vp,
                               ctypes.POINTER(NB200Launch), _vp]),
+    "nb200_rms_norm_host_work_bytes": (_i64, [_int, _i64, _i64]),
+    "nb200_rms_norm_host": (_int, [_vp, _vp, _int, _i64, _i64, _dbl, _vp, _i64, _vp, _i64, _vp]),
     "nb200_segment_spans": (_int, [_vp, _int, _i64, _i64, _int, _i64, _vp, _vp, _vp]),
     "nb200_segment_pool": (_int, [_vp, _int, _i64, _i64, _i64, _i64, _vp, _int, _i64, _i64, _int, _int,
                                   ctypes.c_uint32, _vp, _vp, _vp]),

@@ -285,6 +285,44 @@ def launch_rms_norm(x, gamma, out, *, eps: float, plan="serial", launch=None):
     _lib.check(rc, "neptune rms_norm")
 
 
+def run_rms_norm_host(x, gamma, *, eps: float = 1e-6, out=None, chunk_rows: int = 0, device=None):
+    """RMSNorm of host-resident rows (nb200_rms_norm_host): x [..., ncols] and gamma [ncols] are
+    contiguous CPU tensors (pinned memory lets the copies overlap); the rows stream through the GPU
+    in chunks with copies in both directions overlapping the kernel. Returns `out` (a pinned CPU
+    tensor shaped like x unless given), complete once the device's current stream has been
+    synchronised. Results equal run_rms_norm on the same rows moved to the device."""
+    import torch
+
+    if x.device.type != "cpu" or gamma.device.type != "cpu" or (out is not None and out.device.type != "cpu"):
+        raise ValueError("run_rms_norm_host takes host (CPU) tensors")
+    if x.dtype not in (torch.float32, torch.bfloat16, torch.float16) or gamma.dtype != x.dtype:
+        raise TypeError("run_rms_norm_host: x and gamma must share a float32/bfloat16/float16 dtype")
+    if x.dim() < 1 or gamma.dim() != 1 or gamma.shape[0] != x.shape[-1]:
+        raise ValueError("run_rms_norm_host: gamma must be 1-D with x's last-dimension width")
+    if not (x.is_contiguous() and gamma.is_contiguous()):
+        raise ValueError("run_rms_norm_host: x and gamma must be contiguous")
+    if out is None:
+        out = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+    elif out.shape != x.shape or out.dtype != x.dtype or not out.is_contiguous():
+        raise ValueError("run_rms_norm_host: out must be a contiguous tensor shaped like x")
+    ncols = x.shape[-1]
+    rows = x.numel() // ncols if ncols else 0
+    if rows == 0:
+        return out
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    lib = _lib.load()
+    need = lib.nb200_rms_norm_host_work_bytes(dtype_code(x.dtype), ncols, int(chunk_rows))
+    if need < 0:
+        raise ValueError("run_rms_norm_host: bad width or chunk size")
+    with _on_device(dev):
+        work = torch.empty(need, dtype=torch.uint8, device=dev)
+        rc = lib.nb200_rms_norm_host(_ptr(x), _ptr(gamma), dtype_code(x.dtype), rows, ncols, float(eps),
+                                     _ptr(out), int(chunk_rows), _ptr(work), need,
+                                     ctypes.c_void_p(current_stream(dev)))
+    _lib.check(rc, "neptune rms_norm_host")
+    return out
+
+
 def run_rms_norm(x, gamma, *, eps: float = 1e-6, plan="serial"):
     """Direct structured execution (template.py:322-335): fresh contiguous output."""
     import torch

@@ -86,6 +86,21 @@ def test_argument_validation_happens_before_any_launch():
     odd = ctypes.c_void_p((1 << 20) + 2)
     assert lib.nb200_attention(odd, fake, fake, fake, None, 1, 1, 8, 128, 1, 0.1, null) == L.NB200_ERR_ARG
     assert "aligned" in L.last_error()
+    # host-row RMSNorm: workspace size, then dtype / size / eps / pointer / workspace checks on
+    # the host (before any CUDA call); zero rows is a successful no-op
+    need = lib.nb200_rms_norm_host_work_bytes(1, 4096, 2048)
+    assert need == 8192 + 4 * 2048 * 8192
+    assert lib.nb200_rms_norm_host_work_bytes(1, 4096, 0) == 8192 + 4 * (16 << 20)
+    assert lib.nb200_rms_norm_host_work_bytes(7, 4096, 0) == -1
+    assert lib.nb200_rms_norm_host(fake, fake, 7, 4, 8, 1e-6, fake, 0, fake, need, null) == L.NB200_ERR_ARG
+    assert lib.nb200_rms_norm_host(fake, fake, 1, 4, 0, 1e-6, fake, 0, fake, need, null) == L.NB200_ERR_ARG
+    assert lib.nb200_rms_norm_host(fake, fake, 1, 4, 8, 0.0, fake, 0, fake, need, null) == L.NB200_ERR_ARG
+    assert lib.nb200_rms_norm_host(null, fake, 1, 4, 8, 1e-6, fake, 0, fake, need, null) == L.NB200_ERR_ARG
+    assert lib.nb200_rms_norm_host(fake, fake, 1, 4, 8, 1e-6, fake, 2, odd, need, null) == L.NB200_ERR_ARG
+    assert "aligned" in L.last_error()
+    small = lib.nb200_rms_norm_host_work_bytes(1, 8, 2) - 1
+    assert lib.nb200_rms_norm_host(fake, fake, 1, 4, 8, 1e-6, fake, 2, fake, small, null) == L.NB200_ERR_ARG
+    assert lib.nb200_rms_norm_host(null, null, 1, 0, 8, 1e-6, null, 0, null, 0, null) == L.NB200_OK
 
 
 def test_check_maps_status_to_reference_exceptions():

@@ -260,6 +260,38 @@ def test_rms_norm_matches_oracle_and_golden(oracle_mod):
         assert_rms_close(NB.run_rms_norm(x, g).float().cpu().numpy(), rms[key + "|out"], dtype)
 
 
+def test_host_row_rms_norm_streams_chunks_bit_exactly(oracle_mod):
+    """nb200_rms_norm_host: rows in host memory, chunked through the device with overlapping copies,
+    give bit for bit the device path's rows (and so the oracle's within the RMSNorm bound), for
+    ragged last chunks, one-row chunks, pageable memory and the default chunking."""
+    import torch
+
+    import neptune_opt_b200 as NB
+
+    gen = torch.Generator().manual_seed(23)
+    cases = [((16384, 4096), torch.bfloat16, 0, True), ((1000, 768), torch.float16, 7, True),
+             ((3, 2048), torch.float32, 1, False), ((5, 3, 1000), torch.bfloat16, 4, True),
+             ((2, 512), torch.bfloat16, 4096, False)]
+    for shape, dt, chunk, pinned in cases:
+        x = torch.randn(*shape, generator=gen).to(dt)
+        g = (1 + 0.1 * torch.randn(shape[-1], generator=gen)).to(dt)
+        if pinned:
+            x, g = x.pin_memory(), g.pin_memory()
+        before = x.clone()
+        out = NB.run_rms_norm_host(x, g, eps=1e-6, chunk_rows=chunk)
+        torch.cuda.current_stream().synchronize()
+        want = NB.run_rms_norm(x.cuda(), g.cuda(), eps=1e-6).cpu()
+        assert out.shape == x.shape and out.dtype == dt and torch.equal(x, before)
+        assert torch.equal(out, want), f"{shape} {dt} chunk_rows={chunk}"
+    dtype = "float16"
+    x = torch.randn(257, 1024, generator=gen).half().pin_memory()
+    g = (1 + 0.1 * torch.randn(1024, generator=gen)).half().pin_memory()
+    out = NB.run_rms_norm_host(x, g, eps=1e-6, chunk_rows=16)
+    torch.cuda.current_stream().synchronize()
+    ref = oracle_mod.rms_norm(x.float().numpy(), g.float().numpy(), 1e-6, dtype)
+    assert_rms_close(out.float().numpy(), ref, dtype)
+
+
 def test_segment_pool_bit_exact_on_reference_cases():
     import torch
 
