@@ -1,4 +1,5 @@
-// RMSNorm over rows that live in host memory: the rows stream through the device in chunks, with
+// RMSNorm over rows that live in host memory: the rows stream through the device in chunks (of
+// ramped sizes at both ends, see ramp_rows), with
 // the copy of the next chunk to the device and the copy of the previous chunk back to the host
 // running on two helper streams while the current chunk's kernel runs on the caller's stream.
 // PCIe moves data both ways at once, so a step costs about one direction's transfer time instead
@@ -62,6 +63,19 @@ int64_t chunk_rows_for(int64_t rows, int64_t row_bytes, int64_t chunk_rows) {
     if (chunk_rows <= 0) chunk_rows = kDefaultChunkBytes / row_bytes;
     if (chunk_rows < 1) chunk_rows = 1;
     return chunk_rows < rows ? chunk_rows : rows;
+}
+
+// Rows of chunk k (the k-th from the start) when `remaining` rows are left, with at most c rows per
+// chunk: the first chunks ramp up (c/8, c/4, c/2) so the first copy back starts early, and the
+// last ones halve down to c/8 so the last copy back is short. Both ends of the pipeline then cost
+// a fraction of a full chunk's transfer.
+int64_t ramp_rows(int64_t k, int64_t remaining, int64_t c) {
+    int64_t n = k < 3 ? c >> (3 - k) : c;
+    const int64_t tail = (remaining + 1) / 2;
+    if (n > tail) n = tail;
+    const int64_t floor_rows = c / 8 > 0 ? c / 8 : 1;
+    if (n < floor_rows) n = floor_rows;
+    return n < remaining ? n : remaining;
 }
 
 }  // namespace
@@ -128,10 +142,10 @@ int nb200_rms_norm_host(const void* x, const void* gamma, int dtype, int64_t row
     if (e == cudaSuccess) e = cudaStreamWaitEvent(p.in, p.start, 0);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(p.out, p.start, 0);
     if (e == cudaSuccess) e = cudaMemcpyAsync(gd, gamma, row_bytes, cudaMemcpyHostToDevice, p.in);
-    const int64_t nchunks = (rows + crows - 1) / crows;
-    for (int64_t k = 0; e == cudaSuccess && rc == NB200_OK && k < nchunks; ++k) {
+    int64_t r0 = 0;
+    for (int64_t k = 0; e == cudaSuccess && rc == NB200_OK && r0 < rows; ++k) {
         const int b = (int)(k & 1);
-        const int64_t r0 = k * crows, nr = (rows - r0 < crows) ? rows - r0 : crows;
+        const int64_t nr = ramp_rows(k, rows - r0, crows);
         const size_t bytes = (size_t)(nr * row_bytes);
         if (k >= 2) e = cudaStreamWaitEvent(p.in, p.ran[b], 0);
         if (e == cudaSuccess) e = cudaMemcpyAsync(in[b], xh + r0 * row_bytes, bytes, cudaMemcpyHostToDevice, p.in);
@@ -145,6 +159,7 @@ int nb200_rms_norm_host(const void* x, const void* gamma, int dtype, int64_t row
         if (e == cudaSuccess) e = cudaStreamWaitEvent(p.out, p.ran[b], 0);
         if (e == cudaSuccess) e = cudaMemcpyAsync(yh + r0 * row_bytes, out[b], bytes, cudaMemcpyDeviceToHost, p.out);
         if (e == cudaSuccess) e = cudaEventRecord(p.out_done[b], p.out);
+        r0 += nr;
     }
     // Join: the caller's stream waits for the last copies in both directions, also after an
     // error, so that nothing queued here outlives what the caller's stream orders.
