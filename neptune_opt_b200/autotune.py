@@ -6,9 +6,10 @@ that policy and its vocabulary -- a `(block, num_warps)` pair, `(rows class, pow
 keys, a machine-keyed table holding only measured deviations from the default, a noise margin a
 candidate must clear -- but the pair now selects a CUDA launch:
 
-* ``num_warps == 0``: the library's own policy -- rows that are contiguous and 16-byte aligned are
-  staged through shared memory with bulk copies (each warp owns a ring of stages), others use the
-  register-tiled kernels below;
+* ``num_warps == 0``: the library's own policy -- contiguous, 16-byte aligned rows of 1-8 KB are
+  loaded whole into one warp's registers (several rows per CTA), rows of 8-32 KB are staged through
+  shared memory with bulk copies (each warp owns a ring of stages), others use the register-tiled
+  kernels below;
 * ``num_warps == 1``: one warp folds one row (persistent CTAs of 8 warps, row chunks resident in
   registers, no shared memory or barriers);
 * ``num_warps >= 2``: one CTA of ``32 * num_warps`` threads folds one row (cross-warp reduction
@@ -234,7 +235,10 @@ def op_key(lib: str, name: str, params: dict | None, keepdim: bool,
 
 def search(name: str, rows: int, ncols: int, dtype=None, device: str = "cuda", reps: int = 50,
            candidates=CANDIDATES, params: dict | None = None, warmup: int = 5, rounds: int = 3) -> list:
-    """Time every candidate through the C ABI with CUDA events; fastest first."""
+    """Time every candidate through the C ABI with CUDA events; fastest first.
+
+    Each round replays `reps` launches captured in one CUDA graph, so a small shape measures device
+    time rather than the Python launch path (a candidate that cannot be captured is timed eagerly)."""
     import torch
 
     from neptune_opt_b200 import template
@@ -256,14 +260,154 @@ def search(name: str, rows: int, ncols: int, dtype=None, device: str = "cuda", r
             results.append(Result(block, warps, float("inf")))
             print(f"      block={block} num_warps={warps} cannot launch: {type(exc).__name__}: {exc}")
             continue
+        run = None
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(reps):
+                    launch()
+            run = graph.replay
+        except Exception:  # noqa: BLE001
+            torch.cuda.synchronize()
+
+            def run(launch=launch):
+                for _ in range(reps):
+                    launch()
         times = []
         for _ in range(rounds):
+            run()
             start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             start.record()
-            for _ in range(reps):
-                launch()
+            run()
             end.record()
             end.synchronize()
             times.append(start.elapsed_time(end) / reps)
         results.append(Result(block, warps, min(times)))
     return best_of(results)
+
+
+def choose_many(per_shape: list, default: tuple = DEFAULT, noise: float = NOISE) -> tuple:
+    """One configuration for a bucket measured at several shapes: the candidate whose WORST gain
+    over the default across the shapes is largest (the rule of neptune_codegen/autotune.py:297-356),
+    kept only if that worst case clears `noise`. `per_shape` is a list of measured candidate lists.
+    Returns `(config, worst_case_gain, reason)`."""
+    runs = []
+    for results in per_shape:
+        ms = {(r.block, r.num_warps): r.ms for r in results if math.isfinite(r.ms) and r.ms > 0}
+        if tuple(default) in ms:
+            runs.append(ms)
+    if not runs:
+        return tuple(default), float("nan"), "the default was not measurable: keeping it"
+    shared = set.intersection(*(set(run) for run in runs))
+    scored = sorted(((min(run[tuple(default)] / run[cfg] for run in runs), cfg) for cfg in shared),
+                    key=lambda item: (-item[0], item[1]))
+    worst, cfg = scored[0]
+    if cfg == tuple(default) or worst <= 1.0 + noise:
+        return tuple(default), worst, f"within noise ({worst:.2f}x worst case): keeping the default"
+    return cfg, worst, f"{worst:.2f}x better than the default in the worst case"
+
+
+def measure_shapes(name: str, shapes, dtype=None, device: str = "cuda", reps: int = 50,
+                   candidates=CANDIDATES, rounds: int = 3, params: dict | None = None,
+                   log=print) -> tuple:
+    """Time every candidate at every `(rows, ncols)` shape and reduce each bucket to one choice
+    (neptune_codegen/autotune.py:512-548). Returns `(table, records)`: `table` maps shape keys to
+    configurations and holds only deviations from the default; `records` keeps each shape's
+    measurements."""
+    per_bucket, records = {}, []
+    for rows, ncols in shapes:
+        key = shape_key(rows, ncols)
+        results = search(name, rows, ncols, dtype=dtype, device=device, reps=reps, candidates=candidates,
+                         params=params, rounds=rounds)
+        picked, gain, why = choose(results, DEFAULT)
+        log(f"  rows={rows:6d} ncols={ncols:7d} {key}: " + ", ".join(str(r) for r in results[:3]) +
+            f" -> {picked} ({why})")
+        records.append({"shape": (rows, ncols), "key": key, "picked": picked, "gain": gain,
+                        "results": [(r.block, r.num_warps, r.ms) for r in results]})
+        per_bucket.setdefault(key, []).append(results)
+    out = {}
+    for key, runs in sorted(per_bucket.items()):
+        cfg, worst, why = choose_many(runs, DEFAULT)
+        log(f"  bucket {key} ({len(runs)} shape(s)) -> {cfg}: {why}")
+        if cfg != DEFAULT:
+            out[key] = cfg
+    return out, records
+
+
+def merge_table(all_tables: dict, machine: str, measured_on: str, body: dict, noise: float = NOISE) -> dict:
+    """`all_tables` with `machine`'s entry replaced by a fresh measurement (other machines kept)."""
+    merged = {m: dict(entry) for m, entry in all_tables.items()}
+    merged[machine] = {"measured_on": measured_on, "noise": noise, "table": _valid(body)}
+    return merged
+
+
+def render_tables(all_tables: dict) -> str:
+    """Python source of `launch_table.py` for the given tables (deterministic order)."""
+    lines = ['"""Measured launch configurations for the CUDA folds -- only deviations from',
+             '`autotune.default_config` are listed, keyed by `(rows class, pow2 width bucket)`.',
+             '',
+             'Written by `python -m neptune_opt_b200.autotune --write` (autotune.measure_shapes on the',
+             'machine named in `measured_on`); a machine without an entry uses the default.',
+             '"""',
+             "TABLES = {"]
+    for machine in sorted(all_tables):
+        entry = all_tables[machine]
+        lines.append(f"    {machine!r}: {{")
+        lines.append(f"        'measured_on': {entry.get('measured_on', '')!r},")
+        lines.append(f"        'noise': {float(entry.get('noise', NOISE))!r},")
+        lines.append("        'table': {")
+        for key, cfg in sorted(_valid(entry.get("table", {})).items()):
+            lines.append(f"            {tuple(key)!r}: {tuple(cfg)!r},")
+        lines.append("        },")
+        lines.append("    },")
+    lines.append("}")
+    return "\n".join(lines) + "\n"
+
+
+def write_tables(path: str, all_tables: dict) -> None:
+    with open(path, "w") as f:
+        f.write(render_tables(all_tables))
+
+
+# The measurement campaign: every rows class at widths across the buckets the folds serve, each
+# bucket at two widths (a power of two and a ragged one) so the bucket's choice is a worst case.
+CAMPAIGN_WIDTHS = (256, 1000, 1024, 3000, 4096, 12000, 16384, 50000, 65536, 200000, 262144)
+CAMPAIGN_ROWS = (1, 4, 8, 64, 4096)
+CAMPAIGN_MAX_ELEMS = 1 << 26
+
+
+def campaign_shapes() -> list:
+    shapes = []
+    for ncols in CAMPAIGN_WIDTHS:
+        for rows in CAMPAIGN_ROWS:
+            shapes.append((max(1, min(rows, CAMPAIGN_MAX_ELEMS // ncols)) if rows > THIN_ROWS else rows, ncols))
+    return shapes
+
+
+def main(argv=None) -> int:
+    import argparse
+    import os
+
+    ap = argparse.ArgumentParser(description="Measure the CUDA fold launch table on this GPU.")
+    ap.add_argument("--skeleton", default="logsumexp")
+    ap.add_argument("--dtype", default="float32", choices=("float32", "bfloat16", "float16"))
+    ap.add_argument("--write", action="store_true", help="rewrite launch_table.py with this machine's entry")
+    ap.add_argument("--reps", type=int, default=50)
+    args = ap.parse_args(argv)
+    import torch
+
+    name = torch.cuda.get_device_name(torch.cuda.current_device())
+    machine = machine_key(name)
+    dtype = getattr(torch, args.dtype)
+    print(f"measuring {args.skeleton} ({args.dtype}) on {name} -> table '{machine}'")
+    body, _ = measure_shapes(args.skeleton, campaign_shapes(), dtype=dtype, reps=args.reps)
+    print(f"deviations from the default: {body or 'none'}")
+    if args.write:
+        merged = merge_table(tables(), machine, f"{name}, {args.skeleton} {args.dtype}", body)
+        write_tables(os.path.join(os.path.dirname(os.path.abspath(__file__)), "launch_table.py"), merged)
+        print("launch_table.py written")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

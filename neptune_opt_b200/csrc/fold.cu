@@ -435,8 +435,28 @@ int merge_dispatch(int sk, const nb200_state* states, T* out, int64_t rows, int6
     set_error("unknown dtype %d", dtype);                                             \
     return NB200_ERR_ARG;
 
+// The library's own choice for a fold with no launch given (or variant AUTO), from the launch
+// campaign measured on B200 (autotune.measure_shapes, logsumexp fp32 and bf16, device time):
+// rows under 1 KB fold fastest one per warp from registers (1.2-1.9x over the bulk-copy ring),
+// and fewer rows than SMs of 8-32 KB fastest one per CTA of 8 (<= 16 KB) or 16 warps (1.2-1.7x);
+// the register-row and bulk-copy paths win everywhere else. Returns false to keep the default.
+static bool fold_auto_override(int dtype, int64_t rows, int64_t ncols, nb200_launch& out) {
+    const int64_t rb = ncols * (int64_t)dtype_size(dtype);
+    if (rb < 1024) {
+        out = nb200_launch{NB200_VARIANT_WARP_ROW, 0, 0, 0};
+        return true;
+    }
+    if (rb > 8192 && rb <= 32768 && rows < (int64_t)sm_count()) {
+        out = nb200_launch{NB200_VARIANT_CTA_ROW, rb <= 16384 ? 256 : 512, 0, 0};
+        return true;
+    }
+    return false;
+}
+
 int launch_fold(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t ncols,
                 int64_t srow, int64_t scol, void* out, const nb200_launch* L, cudaStream_t st) {
+    nb200_launch chosen;
+    if ((!L || L->variant == NB200_VARIANT_AUTO) && fold_auto_override(dtype, rows, ncols, chosen)) L = &chosen;
     if (!L || L->variant == NB200_VARIANT_AUTO || L->variant == NB200_VARIANT_STREAM) {
         int rc = stream_fold(sk, p, x, dtype, rows, ncols, srow, scol, out, L, st);
         // rows too wide for a stage: one warp streams each row, when there are enough rows to

@@ -191,6 +191,33 @@ def test_launch_policy_defaults_and_table():
     assert autotune.choose(res, (16384, 0))[0] == (16384, 8)
 
 
+def test_launch_policy_bucket_choice_and_table_writer(tmp_path):
+    R = autotune.Result
+    # a bucket's choice is the best WORST-CASE gain over its shapes, and must clear the noise bar
+    runs = [[R(16384, 0, 1.0), R(16384, 8, 0.5), R(4096, 1, 0.9)],
+            [R(16384, 0, 1.0), R(16384, 8, 0.93), R(4096, 1, 0.8)]]
+    cfg, worst, why = autotune.choose_many(runs)
+    assert cfg == (4096, 1) and abs(worst - 1.0 / 0.9) < 1e-9 and "worst case" in why
+    flat = [[R(16384, 0, 1.0), R(16384, 8, 0.97)], [R(16384, 0, 1.0), R(16384, 8, 0.5)]]
+    assert autotune.choose_many(flat)[0] == autotune.DEFAULT
+    assert autotune.choose_many([[R(16384, 8, 1.0)]])[0] == autotune.DEFAULT  # default unmeasured
+    # a written table round-trips through the module loader and only keeps known candidates
+    merged = autotune.merge_table(autotune.tables(), "test-gpu", "a test",
+                                  {("few", 4096): (16384, 8), ("many", 256): (3, 3)})
+    path = tmp_path / "launch_table.py"
+    autotune.write_tables(str(path), merged)
+    ns = {}
+    exec(path.read_text(), ns)
+    assert ns["TABLES"]["test-gpu"]["table"] == {("few", 4096): (16384, 8)}
+    assert ns["TABLES"]["test-gpu"]["measured_on"] == "a test"
+    assert set(ns["TABLES"]) == set(autotune.tables()) | {"test-gpu"}
+    # the campaign covers every rows class at every width bucket it names, within its size cap
+    shapes = autotune.campaign_shapes()
+    assert {autotune.rows_class(r) for r, _ in shapes} == {"single", "few", "many"}
+    assert all(r * c <= max(autotune.CAMPAIGN_MAX_ELEMS, c * autotune.THIN_ROWS) for r, c in shapes)
+    assert {c for _, c in shapes} == set(autotune.CAMPAIGN_WIDTHS)
+
+
 def test_template_helpers():
     assert template.dtype_code(torch.bfloat16) == 1
     x = torch.randn(2, 3, 8)
