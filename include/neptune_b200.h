@@ -175,6 +175,33 @@ int nb200_fold_merge(int skeleton, const nb200_params* params,
                      int64_t row_stride, int64_t part_stride,
                      void* out, int dtype, void* stream);
 
+/* The split plan across GPUs without a collective (no counterpart in the reference, which has no
+ * multi-GPU path): column shards' chunk states move through NVLink peer memory. Each rank owns an
+ * exchange buffer of nb200_peer_buffer_bytes(rows, world, nparts) bytes (device memory, 256-byte
+ * aligned, ZEROED once before its first use, then reused across calls) and maps every other rank's
+ * buffer with nb200_ipc_handle / nb200_ipc_open (CUDA IPC; the library only maps, it allocates
+ * nothing). Per call, in this order on one stream:
+ *   nb200_fold_partial  -> states[rows][nlocal] of this rank's shard;
+ *   nb200_peer_push     -> writes them into slot `rank` (nparts wide, parts past nlocal empty) of
+ *                          every rank's buffer and raises this rank's flag there (peers[r] = rank
+ *                          r's buffer as mapped here, peers[rank] = buffer);
+ *   nb200_peer_merge    -> waits until every rank's flag has arrived (bounded: about a second, then
+ *                          bit 2 of nb200_stream_fault and the output is left unwritten), merges
+ *                          each row's world * nparts states in ascending (rank, part) order into
+ *                          out[rows] -- the result of nb200_fold_merge on the gathered states.
+ * Every rank makes the same calls in the same order with the same rows and nparts; a call's epoch
+ * lives in the buffer, so the sequence may be captured in a CUDA graph and replayed. world <= 8. */
+int64_t nb200_peer_buffer_bytes(int64_t rows, int64_t world, int64_t nparts);
+int nb200_peer_push(const nb200_state* states, int64_t rows, int64_t nlocal, int64_t nparts,
+                    void* const* peers, int world, int rank, void* buffer, void* stream);
+int nb200_peer_merge(int skeleton, const nb200_params* params, void* buffer, int64_t rows,
+                     int64_t nparts, int world, void* out, int dtype, void* stream);
+/* CUDA IPC of a device allocation: handle (64 bytes) and the byte offset of ptr inside it; open
+ * maps a peer's allocation (base; add the peer's offset), close unmaps it. */
+int nb200_ipc_handle(const void* ptr, void* handle, int64_t* offset);
+int nb200_ipc_open(const void* handle, void** base);
+int nb200_ipc_close(void* base);
+
 /* ------------------------------------------------------------------ a3: RMSNorm
  * out = round_in(x * rsqrt_rn(div_rn(sum x^2, ncols) + eps)) * gamma, rounded to the
  * input dtype; fp32 stages with no contraction (neptune_codegen/emitters.py:549-627,

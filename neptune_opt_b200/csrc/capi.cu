@@ -1,8 +1,11 @@
 // The extern "C" boundary: argument validation, error reporting and launch bookkeeping.
 // Nothing here allocates device memory; every pointer is caller-owned.
+#include <cudaTypedefs.h>
+
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -122,10 +125,11 @@ uint64_t nb200_launch_count(void) { return g_launches.load(std::memory_order_rel
 
 int nb200_stream_fault(uint32_t* bits) {
     if (!bits) { set_error("nb200_stream_fault: null pointer"); return NB200_ERR_ARG; }
-    unsigned int v = 0, w = 0;
+    unsigned int v = 0, w = 0, x = 0;
     int rc = stream_fault_take(&v);
     if (rc == NB200_OK) rc = attn_fault_take(&w);
-    *bits = v | w;
+    if (rc == NB200_OK) rc = peer_fault_take(&x);
+    *bits = v | w | x;
     return rc;
 }
 
@@ -275,6 +279,103 @@ int nb200_segment_pool(const void* data, int dtype, int64_t nrows, int64_t chann
     return launch_segment_pool(data, dtype, nrows, channels, stride_row, stride_channel, bounds, index_dtype,
                                bound_stride, nsegments, reduce, has_initial, initial_bits, out, status,
                                (cudaStream_t)stream);
+}
+
+int64_t nb200_peer_buffer_bytes(int64_t rows, int64_t world, int64_t nparts) {
+    if (rows < 0 || world < 1 || world > peer_max_world() || nparts < 1) return -1;
+    return peer_buffer_bytes(rows, world, nparts);
+}
+
+int nb200_peer_push(const nb200_state* states, int64_t rows, int64_t nlocal, int64_t nparts, void* const* peers,
+                    int world, int rank, void* buffer, void* stream) {
+    if (world < 1 || world > peer_max_world() || rank < 0 || rank >= world) {
+        set_error("nb200_peer_push: need 1 <= world <= %d and 0 <= rank < world", peer_max_world());
+        return NB200_ERR_ARG;
+    }
+    if (rows < 0 || nlocal < 0 || nparts < 1 || nlocal > nparts) {
+        set_error("nb200_peer_push: need rows >= 0 and 0 <= nlocal <= nparts, nparts >= 1");
+        return NB200_ERR_ARG;
+    }
+    if (!peers || !buffer || (rows > 0 && nlocal > 0 && !states)) {
+        set_error("nb200_peer_push: null pointer");
+        return NB200_ERR_ARG;
+    }
+    for (int r = 0; r < world; ++r)
+        if (!peers[r] || (reinterpret_cast<uintptr_t>(peers[r]) & 255u)) {
+            set_error("nb200_peer_push: exchange buffer of rank %d is null or not 256-byte aligned", r);
+            return NB200_ERR_ARG;
+        }
+    if (peers[rank] != buffer) {
+        set_error("nb200_peer_push: peers[rank] must be this rank's own buffer");
+        return NB200_ERR_ARG;
+    }
+    return launch_peer_push(states, rows, nlocal, nparts, peers, world, rank, buffer, (cudaStream_t)stream);
+}
+
+int nb200_peer_merge(int skeleton, const nb200_params* params, void* buffer, int64_t rows, int64_t nparts,
+                     int world, void* out, int dtype, void* stream) {
+    nb200_params q;
+    int rc = check_params(skeleton, params, &q);
+    if (rc) return rc;
+    if (!valid_dtype(dtype)) { set_error("nb200_peer_merge: unsupported dtype %d", dtype); return NB200_ERR_ARG; }
+    if (world < 1 || world > peer_max_world() || rows < 0 || nparts < 1) {
+        set_error("nb200_peer_merge: need 1 <= world <= %d, rows >= 0, nparts >= 1", peer_max_world());
+        return NB200_ERR_ARG;
+    }
+    if (!buffer || (rows > 0 && !out) || (reinterpret_cast<uintptr_t>(buffer) & 255u)) {
+        set_error("nb200_peer_merge: null or unaligned pointer");
+        return NB200_ERR_ARG;
+    }
+    return launch_peer_merge(skeleton, make_params(q, 0), buffer, rows, nparts, world, out, dtype,
+                             (cudaStream_t)stream);
+}
+
+int nb200_ipc_handle(const void* ptr, void* handle, int64_t* offset) {
+    if (!ptr || !handle || !offset) { set_error("nb200_ipc_handle: null pointer"); return NB200_ERR_ARG; }
+    static PFN_cuMemGetAddressRange_v3020 range = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+        cudaGetLastError();
+    });
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (!range || range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) {
+        set_error("nb200_ipc_handle: %p is not device memory this process allocated", ptr);
+        return NB200_ERR_ARG;
+    }
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) {
+        set_error("nb200_ipc_handle: %s", cudaGetErrorString(cudaGetLastError()));
+        return NB200_ERR_LAUNCH;
+    }
+    std::memcpy(handle, &h, sizeof(h));
+    *offset = (int64_t)(reinterpret_cast<uintptr_t>(ptr) - (uintptr_t)base);
+    return NB200_OK;
+}
+
+int nb200_ipc_open(const void* handle, void** base) {
+    if (!handle || !base) { set_error("nb200_ipc_open: null pointer"); return NB200_ERR_ARG; }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    if (cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        set_error("nb200_ipc_open: %s", cudaGetErrorString(cudaGetLastError()));
+        return NB200_ERR_LAUNCH;
+    }
+    return NB200_OK;
+}
+
+int nb200_ipc_close(void* base) {
+    if (!base) { set_error("nb200_ipc_close: null pointer"); return NB200_ERR_ARG; }
+    if (cudaIpcCloseMemHandle(base) != cudaSuccess) {
+        set_error("nb200_ipc_close: %s", cudaGetErrorString(cudaGetLastError()));
+        return NB200_ERR_LAUNCH;
+    }
+    return NB200_OK;
 }
 
 int nb200_attention(const void* q, const void* k, const void* v, void* o, float* lse, int64_t batch,

@@ -201,9 +201,36 @@ __device__ __forceinline__ St shfl_state(const St& s, int o) {
     return r;
 }
 
-// One warp per row. Lane l folds the contiguous run of parts [l*k, (l+1)*k) left to right; the
-// 32 runs then combine in a fixed balanced tree, always with the lower-indexed run on the left.
-// The order depends only on nparts, so the result is deterministic.
+// One row's states merged by a warp. Lane l folds the contiguous run of parts [l*k, (l+1)*k) left
+// to right; the 32 runs then combine in a fixed balanced tree, always with the lower-indexed run on
+// the left. The order depends only on nparts, so the result is deterministic. kL2 reads the states
+// at L2 (states another GPU wrote into this one's memory).
+template <int S, bool kL2>
+__device__ __forceinline__ St merge_row(const nb200_state* row, int64_t nparts, int64_t pstride, int lane,
+                                        const Params& p) {
+    const int64_t k = (nparts + 31) / 32;
+    St s = empty_state();
+    const int64_t lo = (int64_t)lane * k;
+    const int64_t hi = min(lo + k, nparts);
+    for (int64_t j = lo; j < hi; ++j) {
+        nb200_state b;
+        if constexpr (kL2) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(row + j * pstride));
+            b = nb200_state{v.x, v.y, __float_as_int(v.z), __float_as_int(v.w)};
+        } else {
+            b = row[j * pstride];
+        }
+        s = merge<S>(s, St{b.m, b.acc, b.seen, b.status}, p);
+    }
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const St other = shfl_state(s, o);
+        s = (lane & o) ? merge<S>(other, s, p) : merge<S>(s, other, p);
+    }
+    return s;
+}
+
+// One warp per row.
 template <int S, typename T>
 __global__ void __launch_bounds__(256)
 merge_kernel(const nb200_state* __restrict__ states, T* __restrict__ out, int64_t rows,
@@ -213,21 +240,113 @@ merge_kernel(const nb200_state* __restrict__ states, T* __restrict__ out, int64_
     const int lane = threadIdx.x & 31;
     const int64_t gid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int64_t ng = (int64_t)gridDim.x * (blockDim.x >> 5);
-    const int64_t k = (nparts + 31) / 32;
     for (int64_t r = gid; r < rows; r += ng) {
-        St s = empty_state();
-        const int64_t lo = (int64_t)lane * k;
-        const int64_t hi = min(lo + k, nparts);
-        for (int64_t j = lo; j < hi; ++j) {
-            const nb200_state b = states[r * rstride + j * pstride];
-            s = merge<S>(s, St{b.m, b.acc, b.seen, b.status}, p);
-        }
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const St other = shfl_state(s, o);
-            s = (lane & o) ? merge<S>(other, s, p) : merge<S>(s, other, p);
-        }
+        const St s = merge_row<S, false>(states + r * rstride, nparts, pstride, lane, p);
         if (lane == 0) out[r] = Elem<T>::from_f(finalize<S>(s, p));
+    }
+}
+
+// ------------------------------------------------------------------ split plan across GPUs
+// The column-sharded split plan exchanges its chunk states through peer memory instead of a
+// collective. Each rank owns an exchange buffer, mapped into every other rank's address space:
+//   header   epoch of the last completed exchange, two completion counters, flag[r] = the last
+//            epoch rank r has delivered here;
+//   slots    two parities x [rows][world][nparts] states; call e uses parity e & 1.
+// Call e: peer_push_kernel writes this rank's states into slot `rank` of parity e & 1 in every
+// rank's buffer (stores over NVLink), and its last CTA raises flag[rank] = e in every buffer
+// (after a system-scope fence). peer_merge_kernel waits until every flag has reached e (bounded),
+// merges each row's world * nparts states in ascending (rank, part) order -- the order of the
+// single-GPU split plan -- and its last CTA records e as completed. A rank can be at most one call
+// ahead of another (its next push follows its own merge, which needs everyone's flag), so two
+// parities keep a fast rank from overwriting states a slow one is still merging. The epoch lives
+// in device memory, so a captured CUDA graph replays correctly.
+static __device__ unsigned int g_peer_fault = 0u;
+constexpr int kMaxPeers = 8;
+constexpr int64_t kPeerHeaderBytes = 256;
+constexpr long long kPeerWaitCycles = 1ll << 31;
+struct PeerHeader {
+    unsigned int ep;          // epoch of the last completed exchange on this rank
+    unsigned int push_done;   // CTAs of the current push that have finished (reset by the last)
+    unsigned int merge_done;  // the same for the merge
+    unsigned int pad;
+    unsigned int flag[kMaxPeers];
+};
+static_assert(sizeof(PeerHeader) <= kPeerHeaderBytes, "peer header");
+struct PeerPtrs {
+    unsigned char* p[kMaxPeers];  // every rank's exchange buffer as mapped in this process
+};
+
+__global__ void __launch_bounds__(256)
+peer_push_kernel(const nb200_state* __restrict__ states, int64_t rows, int64_t nlocal, int64_t nparts,
+                 PeerPtrs peers, int world, int rank, unsigned char* own) {
+    pdl_wait();
+    pdl_trigger();
+    PeerHeader* h = reinterpret_cast<PeerHeader*>(own);
+    const unsigned int e = *reinterpret_cast<volatile unsigned int*>(&h->ep) + 1u;
+    const int64_t par = e & 1u, n = rows * nparts;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = i / nparts, part = i - row * nparts;
+        // parts past this rank's own count are empty states (unequal shard widths)
+        const float4 v = part < nlocal ? reinterpret_cast<const float4*>(states)[row * nlocal + part]
+                                       : make_float4(-NB200_INF, 0.f, 0.f, 0.f);
+        const int64_t slot = ((par * rows + row) * world + rank) * nparts + part;
+        for (int r = 0; r < world; ++r)
+            reinterpret_cast<float4*>(peers.p[r] + kPeerHeaderBytes)[slot] = v;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(&h->push_done, 1u) == gridDim.x - 1) {
+        atomicExch(&h->push_done, 0u);
+        __threadfence_system();
+        for (int r = 0; r < world; ++r) {
+            unsigned int* f = &reinterpret_cast<PeerHeader*>(peers.p[r])->flag[rank];
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
+        }
+    }
+}
+
+template <int S, typename T>
+__global__ void __launch_bounds__(256)
+peer_merge_kernel(unsigned char* own, T* __restrict__ out, int64_t rows, int64_t nparts, int world, Params p) {
+    pdl_wait();
+    pdl_trigger();
+    PeerHeader* h = reinterpret_cast<PeerHeader*>(own);
+    const unsigned int e = *reinterpret_cast<volatile unsigned int*>(&h->ep) + 1u;
+    __shared__ int arrived;
+    if (threadIdx.x == 0) {
+        bool ok = true;
+        const long long t0 = clock64();
+        for (int r = 0; r < world && ok; ++r) {
+            for (unsigned int it = 0;; ++it) {
+                unsigned int f;
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(&h->flag[r]) : "memory");
+                if ((int)(f - e) >= 0) break;
+                if ((it & 63u) == 63u && clock64() - t0 > kPeerWaitCycles) {
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        if (!ok) atomicOr(&g_peer_fault, 4u);
+        arrived = ok;
+    }
+    __syncthreads();
+    if (arrived) {
+        const int lane = threadIdx.x & 31;
+        const int64_t total = (int64_t)world * nparts;
+        const nb200_state* slots =
+            reinterpret_cast<const nb200_state*>(own + kPeerHeaderBytes) + (int64_t)(e & 1u) * rows * total;
+        const int64_t gid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+        const int64_t ng = (int64_t)gridDim.x * (blockDim.x >> 5);
+        for (int64_t r = gid; r < rows; r += ng) {
+            const St s = merge_row<S, true>(slots + r * total, total, 1, lane, p);
+            if (lane == 0) out[r] = Elem<T>::from_f(finalize<S>(s, p));
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(&h->merge_done, 1u) == gridDim.x - 1) {
+        atomicExch(&h->merge_done, 0u);
+        atomicExch(&h->ep, e);
     }
 }
 
@@ -413,6 +532,25 @@ int partial_dispatch(int sk, const T* x, nb200_state* states, int64_t rows, int6
 }
 
 template <typename T>
+int peer_merge_dispatch(int sk, unsigned char* own, T* out, int64_t rows, int64_t nparts, int world,
+                        const Params& p, cudaStream_t st) {
+    switch (sk) {
+#define X(S)                                                                       \
+    case S: {                                                                      \
+        auto k = peer_merge_kernel<S, T>;                                          \
+        const int g = persistent_grid(k, 256, 0, (rows + 7) / 8, 0);               \
+        launch_pdl(k, g, 256, 0, st, own, out, rows, nparts, world, p);            \
+        count_launch();                                                            \
+        return finish_launch("nb200_peer_merge");                                  \
+    }
+        NB200_SPLIT_SKELETONS(X)
+#undef X
+    }
+    set_error("skeleton %d has no split plan (two-pass skeletons need extended carried state)", sk);
+    return NB200_ERR_UNSUPPORTED;
+}
+
+template <typename T>
 int merge_dispatch(int sk, const nb200_state* states, T* out, int64_t rows, int64_t nparts,
                    int64_t rs, int64_t ps, const Params& p, cudaStream_t st) {
     switch (sk) {
@@ -509,6 +647,40 @@ int launch_partial(int sk, const Params& p, const void* x, int dtype, int64_t ro
 int launch_merge(int sk, const Params& p, const nb200_state* states, int64_t rows, int64_t nparts,
                  int64_t rs, int64_t ps, void* out, int dtype, cudaStream_t st) {
     NB200_DTYPE_CASES(dtype, merge_dispatch<T>(sk, states, (T*)out, rows, nparts, rs, ps, p, st))
+}
+
+int64_t peer_buffer_bytes(int64_t rows, int64_t world, int64_t nparts) {
+    return kPeerHeaderBytes + 2 * rows * world * nparts * (int64_t)sizeof(nb200_state);
+}
+
+int peer_max_world() { return kMaxPeers; }
+
+int launch_peer_push(const nb200_state* states, int64_t rows, int64_t nlocal, int64_t nparts, void* const* peers,
+                     int world, int rank, void* own, cudaStream_t st) {
+    PeerPtrs pp{};
+    for (int r = 0; r < world; ++r) pp.p[r] = static_cast<unsigned char*>(peers[r]);
+    const int g = persistent_grid(peer_push_kernel, 256, 0, (rows * nparts + 255) / 256, 0);
+    launch_pdl(peer_push_kernel, g, 256, 0, st, states, rows, nlocal, nparts, pp, world, rank,
+               static_cast<unsigned char*>(own));
+    count_launch();
+    return finish_launch("nb200_peer_push");
+}
+
+int launch_peer_merge(int sk, const Params& p, void* own, int64_t rows, int64_t nparts, int world, void* out,
+                      int dtype, cudaStream_t st) {
+    NB200_DTYPE_CASES(dtype, peer_merge_dispatch<T>(sk, static_cast<unsigned char*>(own), (T*)out, rows, nparts,
+                                                    world, p, st))
+}
+
+int peer_fault_take(unsigned int* bits) {
+    unsigned int v = 0, zero = 0;
+    if (cudaMemcpyFromSymbol(&v, g_peer_fault, sizeof(v)) != cudaSuccess ||
+        cudaMemcpyToSymbol(g_peer_fault, &zero, sizeof(zero)) != cudaSuccess) {
+        set_error("cannot read the peer-exchange fault word: %s", cudaGetErrorString(cudaGetLastError()));
+        return NB200_ERR_LAUNCH;
+    }
+    *bits = v;
+    return NB200_OK;
 }
 
 }  // namespace nb200

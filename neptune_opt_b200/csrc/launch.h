@@ -24,6 +24,15 @@ int launch_partial(int sk, const Params& p, const void* x, int dtype, int64_t ro
 int launch_merge(int sk, const Params& p, const nb200_state* states, int64_t rows, int64_t nparts,
                  int64_t rs, int64_t ps, void* out, int dtype, cudaStream_t st);
 
+// Column-sharded split plan across GPUs: chunk states exchanged through peer memory (fold.cu).
+int64_t peer_buffer_bytes(int64_t rows, int64_t world, int64_t nparts);
+int peer_max_world();
+int launch_peer_push(const nb200_state* states, int64_t rows, int64_t nlocal, int64_t nparts, void* const* peers,
+                     int world, int rank, void* own, cudaStream_t st);
+int launch_peer_merge(int sk, const Params& p, void* own, int64_t rows, int64_t nparts, int world, void* out,
+                      int dtype, cudaStream_t st);
+int peer_fault_take(unsigned int* bits);
+
 int launch_rms(const void* x, const void* gamma, int dtype, int64_t rows, int64_t ncols,
                int64_t srow, int64_t scol, int64_t sg, float eps, void* out,
                const nb200_launch* L, cudaStream_t st);

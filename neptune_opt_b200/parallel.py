@@ -11,8 +11,10 @@ partitions into independent units, so ranks need no data-path collective:
 
 The one exchange is the split plan for ultra-wide rows when the reduction axis itself is sharded
 across GPUs (`sharded_split_fold`): each rank folds its column shard into per-row chunk states
-(16 bytes each), one all-gather moves them (a few KB per rank), and every rank merges them in
-ascending (rank, chunk) order -- the same certified order as the single-GPU split plan.
+(16 bytes each) and every rank merges all of them in ascending (rank, chunk) order -- the same
+certified order as the single-GPU split plan. The states move either through one all-gather or,
+with a `PeerExchange`, through NVLink peer memory: the pushing kernel stores them into every rank's
+buffer and raises a flag, the merging kernel waits for all flags (no collective, no host step).
 """
 from __future__ import annotations
 
@@ -122,8 +124,104 @@ def _cuda_merge(name, params, states, out):
     return out
 
 
+class PeerExchange:
+    """Exchange buffers of the column-sharded split plan, mapped across the ranks of `group`.
+
+    Every rank allocates one zeroed buffer of `nb200_peer_buffer_bytes(rows, world, nparts)` bytes on
+    its GPU and maps the others' with CUDA IPC (handles swapped once with all_gather_object). A
+    `sharded_split_fold(..., exchange=ex)` call then moves the chunk states with two kernels --
+    stores into every peer's buffer plus a flag, and a merge that waits for all flags -- instead of
+    a collective. `nparts` is the per-rank slot width: the largest number of chunks any rank's shard
+    has. Create it on every rank of the group (it synchronises them) and `close()` it on every rank.
+    """
+
+    def __init__(self, rows: int, nparts: int, group=None, device=None):
+        import torch
+        import torch.distributed as td
+
+        from neptune_opt_b200 import _lib
+
+        self.group = group
+        self.world = td.get_world_size(group)
+        self.rank = td.get_rank(group)
+        self.rows, self.nparts = int(rows), int(nparts)
+        self._lib = lib = _lib.load()
+        self._opened, self.peers = [], None
+        nbytes = int(lib.nb200_peer_buffer_bytes(self.rows, self.world, self.nparts))
+        if nbytes < 0:
+            raise ValueError(f"no peer exchange for rows={rows}, world={self.world}, nparts={nparts} (world <= 8)")
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self._storage = torch.zeros(nbytes + 256, dtype=torch.uint8, device=device)
+        pad = (-self._storage.data_ptr()) % 256
+        self.buffer = self._storage[pad:pad + nbytes]
+        handle = (ctypes.c_char * 64)()
+        offset = ctypes.c_int64()
+        _lib.check(lib.nb200_ipc_handle(ctypes.c_void_p(self.buffer.data_ptr()), handle, ctypes.byref(offset)),
+                   "peer exchange handle")
+        torch.cuda.synchronize(device)  # the buffer is zero before any peer can write into it
+        everyone = [None] * self.world
+        td.all_gather_object(everyone, (bytes(handle), int(offset.value), self.rows, self.nparts), group=group)
+        # Every rank writes into every other rank's buffer at offsets computed from (rows, nparts):
+        # the layouts must agree before anything is mapped (all ranks see the same list and agree).
+        layouts = {(rows_r, parts_r) for _, _, rows_r, parts_r in everyone}
+        if len(layouts) != 1:
+            raise ValueError(f"ranks disagree on the exchange layout (rows, nparts): {sorted(layouts)}")
+        ptrs = []
+        try:
+            for r, (h, off, _, _) in enumerate(everyone):
+                if r == self.rank:
+                    ptrs.append(self.buffer.data_ptr())
+                    continue
+                base = ctypes.c_void_p()
+                _lib.check(lib.nb200_ipc_open(h, ctypes.byref(base)), f"peer exchange: map rank {r}")
+                self._opened.append(base.value)
+                ptrs.append(base.value + off)
+        finally:
+            td.barrier(group=group)  # every rank has mapped every buffer before the first push
+        self.peers = (ctypes.c_void_p * self.world)(*ptrs)
+
+    def exchange_and_merge(self, name, params, states, out):
+        """Push this rank's states [rows, nlocal, 4] and merge all ranks' into out[rows]."""
+        from neptune_opt_b200 import _lib
+        from neptune_opt_b200.skeletons import SKELETONS, checked_params
+        from neptune_opt_b200.template import _on_device, current_stream, dtype_code
+
+        if self.peers is None:
+            raise RuntimeError("the peer exchange is closed")
+        rows, nlocal = states.shape[0], states.shape[1]
+        if rows != self.rows or nlocal > self.nparts:
+            raise ValueError(f"states [{rows}, {nlocal}] do not fit the exchange ({self.rows} rows, "
+                             f"{self.nparts} parts per rank)")
+        p = _lib.params_struct(checked_params(name, params))
+        lib = self._lib
+        with _on_device(states.device):
+            stream = ctypes.c_void_p(current_stream(states.device))
+            _lib.check(lib.nb200_peer_push(ctypes.c_void_p(states.data_ptr()), rows, nlocal, self.nparts,
+                                           self.peers, self.world, self.rank,
+                                           ctypes.c_void_p(self.buffer.data_ptr()), stream), "peer push")
+            _lib.check(lib.nb200_peer_merge(SKELETONS[name].id, ctypes.byref(p),
+                                            ctypes.c_void_p(self.buffer.data_ptr()), rows, self.nparts,
+                                            self.world, ctypes.c_void_p(out.data_ptr()), dtype_code(out.dtype),
+                                            stream), "peer merge")
+        return out
+
+    def close(self):
+        """Unmap the peers' buffers (collective: no rank may still be writing into another's)."""
+        import torch
+        import torch.distributed as td
+
+        if self.peers is None:
+            return
+        torch.cuda.synchronize(self.buffer.device)
+        td.barrier(group=self.group)
+        for base in self._opened:
+            self._lib.nb200_ipc_close(ctypes.c_void_p(base))
+        self._opened = []
+        self.peers = None
+
+
 def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: int = 16384, group=None,
-                       partial_fn=None, merge_fn=None, widths=None):
+                       partial_fn=None, merge_fn=None, widths=None, exchange=None):
     """Fold rows whose columns are sharded across the ranks of `group`, rank order = column order.
 
     Each rank passes its own [rows, width_r] block (the ranks' blocks concatenated along columns in
@@ -135,7 +233,9 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
     `merge_fn(name, params, states, out)` default to the CUDA kernels; tests on CPU ranks substitute
     their own to exercise the sharding and exchange logic. `widths` (every rank's shard width, in
     rank order) skips the width exchange -- and its host synchronisation -- when the caller knows
-    the layout, as a steady-state loop does.
+    the layout, as a steady-state loop does. With `exchange` (a PeerExchange whose slot width is the
+    largest rank's chunk count) the states move through NVLink peer memory instead of an
+    all-gather; the result is the same bit for bit.
     """
     import torch
     import torch.distributed as td
@@ -163,6 +263,12 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
     col_begin = sum(all_widths[:rank])
     max_parts = max(-(-w // chunk) for w in all_widths)
     local = partial_fn(name, params, x_shard, col_begin, ncols_total, chunk)
+    if exchange is not None:
+        if exchange.nparts != max_parts or exchange.world != world:
+            raise ValueError(f"the exchange holds {exchange.nparts} parts per rank for {exchange.world} ranks; "
+                             f"this layout needs {max_parts} for {world}")
+        out = torch.empty(rows, dtype=x_shard.dtype, device=x_shard.device)
+        return exchange.exchange_and_merge(name, params, local, out)
     if local.shape[1] < max_parts:  # pad with empty (seen = 0) states
         pad = torch.zeros(rows, max_parts - local.shape[1], 4, dtype=local.dtype, device=local.device)
         pad[..., 0] = torch.tensor(float("-inf")).view(torch.int32) if local.dtype == torch.int32 else 0

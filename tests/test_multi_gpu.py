@@ -1,12 +1,16 @@
-"""Two-GPU NCCL run of the column-sharded split plan (the one multi-GPU path with an exchange).
+"""Two-GPU run of the column-sharded split plan (the one multi-GPU path with an exchange).
 
-Each rank folds its column shard of a bf16 [64, 100000] block into chunk states, one NCCL
-all-gather exchanges them and every rank merges them in ascending (rank, chunk) order. The result
-must equal, bit for bit, the single-GPU merge of the same states in the same order, and match the
-oracle within 1 bf16 ulp. Runs as two spawned processes; skipped with fewer than two GPUs.
+Each rank folds its column shard of a bf16 [64, 100000] block into chunk states; they move either
+through one NCCL all-gather or through NVLink peer memory (PeerExchange: stores into every rank's
+buffer, a flag per rank, a merge that waits for all flags), and every rank merges them in ascending
+(rank, chunk) order. Both must equal, bit for bit, the single-GPU merge of the same states in the
+same order, match the oracle within 1 bf16 ulp, agree with each other on inputs that change from
+call to call, and replay from a captured CUDA graph. Runs as two spawned processes; skipped with
+fewer than two GPUs.
 """
 from __future__ import annotations
 
+import ctypes
 import os
 import socket
 
@@ -31,7 +35,8 @@ def _rank_main(rank, world, port, result_path):
     import torch
     import torch.distributed as td
 
-    from neptune_opt_b200.parallel import shard_rows, sharded_split_fold
+    from neptune_opt_b200 import _lib
+    from neptune_opt_b200.parallel import PeerExchange, shard_rows, sharded_split_fold
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
@@ -45,9 +50,42 @@ def _rank_main(rank, world, port, result_path):
         out = sharded_split_fold("logsumexp", shard, NCOLS, params={"tiny": 0.0}, chunk=CHUNK)
         widths = [shard_rows(NCOLS, world, r)[1] - shard_rows(NCOLS, world, r)[0] for r in range(world)]
         again = sharded_split_fold("logsumexp", shard, NCOLS, params={"tiny": 0.0}, chunk=CHUNK, widths=widths)
+        # the same through NVLink peer memory: every call equals the all-gather path bit for bit,
+        # with inputs that change from call to call (a stale epoch or parity would show), then
+        # captured in a CUDA graph and replayed
+        ex = PeerExchange(ROWS, max(-(-w // CHUNK) for w in widths))
+        try:
+            peer_ok = []
+            for i in range(5):
+                xi = shard * (1.0 + 0.25 * i)
+                want = sharded_split_fold("logsumexp", xi, NCOLS, params={"tiny": 0.0}, chunk=CHUNK, widths=widths)
+                got = sharded_split_fold("logsumexp", xi, NCOLS, params={"tiny": 0.0}, chunk=CHUNK, widths=widths,
+                                         exchange=ex)
+                peer_ok.append(bool(torch.equal(want, got)))
+            first = sharded_split_fold("logsumexp", shard, NCOLS, params={"tiny": 0.0}, chunk=CHUNK, widths=widths,
+                                       exchange=ex)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                with torch.cuda.graph(graph):
+                    replayed = sharded_split_fold("logsumexp", shard, NCOLS, params={"tiny": 0.0}, chunk=CHUNK,
+                                                  widths=widths, exchange=ex)
+            graph_ok = []
+            for _ in range(3):
+                graph.replay()
+                torch.cuda.synchronize()
+                graph_ok.append(bool(torch.equal(replayed, out)))
+            del graph
+            faults = ctypes.c_uint32(0)
+            _lib.check(_lib.load().nb200_stream_fault(ctypes.byref(faults)), "fault word")
+        finally:
+            ex.close()
         torch.cuda.synchronize()
         if rank == 0:
-            torch.save({"out": out.cpu(), "again": again.cpu()}, result_path)
+            torch.save({"out": out.cpu(), "again": again.cpu(), "peer": first.cpu(), "peer_ok": peer_ok,
+                        "graph_ok": graph_ok, "faults": int(faults.value)}, result_path)
         td.barrier()
     finally:
         td.destroy_process_group()
@@ -91,5 +129,9 @@ def test_sharded_split_over_nccl_matches_single_gpu(tmp_path, oracle_mod):
     merged = _cuda_merge("logsumexp", {"tiny": 0.0}, torch.cat(states, dim=1).contiguous(),
                          torch.empty(ROWS, dtype=torch.bfloat16, device="cuda"))
     assert torch.equal(got["out"], merged.cpu()) and torch.equal(got["again"], merged.cpu())
+    assert torch.equal(got["peer"], merged.cpu()), "peer-memory exchange differs from the merged states"
+    assert all(got["peer_ok"]), f"peer exchange differs from the all-gather path on calls {got['peer_ok']}"
+    assert all(got["graph_ok"]), f"graph replays of the peer exchange differ: {got['graph_ok']}"
+    assert got["faults"] == 0, f"fault word {got['faults']:#x}"
     ref = oracle_mod.fold("logsumexp", x.float().numpy(), {"tiny": 0.0})
     assert_close_dtype(got["out"].float().numpy(), ref, "bfloat16")

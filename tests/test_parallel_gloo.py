@@ -103,6 +103,60 @@ def test_sharded_split_fold_matches_single_process(name, params, uneven):
     np.testing.assert_array_equal(outs[0][0], outs[1][0])
 
 
+def _exchange_worker(rank, world, rows, ncols, chunk):
+    """sharded_split_fold's exchange branch with a stand-in for PeerExchange that moves the states
+    with gloo: the local states, padded to the slot width, must merge to the all-gather result."""
+    import oracle
+    import torch.distributed as td
+
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal((rows, ncols)) * 3).astype(np.float32)
+    cuts = [0, ncols // 3, ncols]
+    lo, hi = cuts[rank], cuts[rank + 1]
+    widths = [cuts[r + 1] - cuts[r] for r in range(world)]
+    nparts = max(-(-w // chunk) for w in widths)
+
+    def partial_fn(nm, prm, x_shard, col_begin, ncols_total, ch):
+        st = oracle.partial(nm, x, prm, col_begin, x_shard.shape[1], ch)
+        return torch.from_numpy(st.view(np.int32).reshape(rows, -1, 4).copy())
+
+    def merge_fn(nm, prm, states, out):
+        st = states.contiguous().numpy().view(oracle.STATE_DTYPE).reshape(rows, -1)
+        out.copy_(torch.from_numpy(oracle.merge(nm, st, prm)))
+        return out
+
+    class GlooExchange:
+        def __init__(self, parts):
+            self.world, self.nparts, self.calls = world, parts, 0
+
+        def exchange_and_merge(self, name, params, states, out):
+            self.calls += 1
+            pad = torch.zeros(rows, self.nparts - states.shape[1], 4, dtype=torch.int32)
+            pad[..., 0] = torch.tensor(float("-inf")).view(torch.int32)
+            mine = torch.cat([states, pad], dim=1)
+            every = [torch.empty_like(mine) for _ in range(world)]
+            td.all_gather(every, mine)
+            return merge_fn(name, params, torch.cat(every, dim=1), out)
+
+    shard = torch.from_numpy(x[:, lo:hi].copy())
+    kw = dict(params={"tiny": 0.0}, chunk=chunk, partial_fn=partial_fn, merge_fn=merge_fn, widths=widths)
+    ref = parallel.sharded_split_fold("logsumexp", shard, ncols, **kw)
+    ex = GlooExchange(nparts)
+    got = parallel.sharded_split_fold("logsumexp", shard, ncols, exchange=ex, **kw)
+    refused = False
+    try:
+        parallel.sharded_split_fold("logsumexp", shard, ncols, exchange=GlooExchange(nparts + 1), **kw)
+    except ValueError:
+        refused = True
+    return ref.numpy(), got.numpy(), ex.calls, refused
+
+
+def test_sharded_split_fold_exchange_branch_matches_all_gather():
+    for ref, got, calls, refused in _run(2, _exchange_worker, 8, 3000, 512):
+        np.testing.assert_array_equal(ref, got)
+        assert calls == 1 and refused
+
+
 def _segment_worker(rank, world, T, nseg, channels):
     import oracle
 
