@@ -329,26 +329,39 @@ def make_attention(torch, NB, seed, causal=False, batch=8):
                     f"{'causal' if causal else 'non-causal'} -> o bf16, lse fp32 (inputs {3 * b * h * s * d * 2 >> 20} MiB > L2)"}
 
 
-def make_sharded_split(torch, NB, seed, dist):
+def make_sharded_split(torch, NB, seed, dist, peer=False):
     """BASELINE config 3b across GPUs: the columns of bf16 [512, 262144] split into one shard per
-    rank; each rank folds its shard into 16K-column chunk states, one NCCL all-gather moves the
-    states (16 B each), every rank merges them in ascending (rank, chunk) order. Total work is fixed
+    rank; each rank folds its shard into 16K-column chunk states, which move to every rank -- one
+    NCCL all-gather, or (peer=True) stores into every rank's exchange buffer over NVLink with a flag
+    per rank -- and every rank merges them in ascending (rank, chunk) order. Total work is fixed
     (strong scaling)."""
-    from neptune_opt_b200.parallel import sharded_split_fold
+    from neptune_opt_b200.parallel import PeerExchange, sharded_split_fold
 
     rows, ncols, block = 512, 262144, 16384
     n = dist.world
     width = ncols // n
     g = torch.Generator(device="cuda").manual_seed(seed)
     xs = [(torch.randn(rows, width, device="cuda", generator=g) * 3.0).to(torch.bfloat16) for _ in range(2)]
+    ex = None
+    if peer:
+        try:  # set-up decides on every rank together (it raises on all ranks or on none)
+            ex = PeerExchange(rows, -(-width // block))
+        except Exception as exc:  # noqa: BLE001
+            if dist.rank == 0:
+                print(f"peer exchange unavailable, region skipped: {exc}", file=sys.stderr, flush=True)
+            return None
 
     def step(i):
-        sharded_split_fold("logsumexp", xs[i % 2], ncols, params={"tiny": 0.0}, chunk=block, widths=[width] * n)
+        sharded_split_fold("logsumexp", xs[i % 2], ncols, params={"tiny": 0.0}, chunk=block, widths=[width] * n,
+                           exchange=ex)
 
-    return {"name": "wide_logsumexp_split_sharded", "step": step, "bytes": rows * ncols * 2 + rows * 2, "rows": rows,
-            "launches": 2, "buffers": 2,
+    how = ("states stored into every rank's exchange buffer over NVLink, one flag per rank, merge waits "
+           "for all flags" if peer else "states all-gathered over NCCL")
+    return {"name": "wide_logsumexp_split_sharded" + ("_peer" if peer else ""), "step": step,
+            "bytes": rows * ncols * 2 + rows * 2, "rows": rows, "launches": 3 if peer else 2, "buffers": 2,
+            "exchange": ex,
             "desc": f"logsumexp bf16 x[{rows},{ncols}] N(0,3^2), columns sharded over {n} GPUs ({width} each), "
-                    f"{block}-column chunk states all-gathered over NCCL and merged in rank order"}
+                    f"{block}-column chunk states {how}, merged in rank order"}
 
 
 def gpu_id(torch) -> str:
@@ -450,7 +463,7 @@ def time_collective_steps(torch, dist, step, steps, warmup):
     torch.cuda.synchronize()
     dist.barrier()
     del g
-    how = ("CUDA graph (partial, NCCL all-gather, merge captured together)" if graph
+    how = ("CUDA graph (the step's kernels and collectives captured together)" if graph
            else "eager (graph capture was not possible on every rank)") + ", max over ranks"
     return dist.max(start.elapsed_time(end) / steps), how
 
@@ -617,15 +630,19 @@ def main():
                 "l2_rotation_buffers": r["buffers"]}
             del r
             torch.cuda.empty_cache()
-        if n > 1:
-            r = make_sharded_split(torch, NB, 2600, dist)
+        for peer in ((False, True) if n > 1 else ()):
+            r = make_sharded_split(torch, NB, 2600, dist, peer=peer)
+            if r is None:
+                continue
             steps = min(args.steps, 50)
             sms_, how = time_collective_steps(torch, dist, r["step"], steps, max(3, args.warmup))
             regions[r["name"]] = {
                 "workload": r["desc"], "ms_per_step": round(sms_, 5), "scaling": "strong",
                 "GB_per_s": round(r["bytes"] / (sms_ * 1e-3) / 1e9, 1),
                 "rows_per_s": round(r["rows"] / (sms_ * 1e-3), 1), "timing": how,
-                "algorithmic_bytes_per_step": r["bytes"]}
+                "algorithmic_bytes_per_step": r["bytes"], "launches_per_step": r["launches"]}
+            if r["exchange"] is not None:
+                r["exchange"].close()
             del r
             torch.cuda.empty_cache()
         for causal in (False, True):

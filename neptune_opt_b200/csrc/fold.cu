@@ -253,8 +253,8 @@ merge_kernel(const nb200_state* __restrict__ states, T* __restrict__ out, int64_
 //            epoch rank r has delivered here;
 //   slots    two parities x [rows][world][nparts] states; call e uses parity e & 1.
 // Call e: peer_push_kernel writes this rank's states into slot `rank` of parity e & 1 in every
-// rank's buffer (stores over NVLink), and its last CTA raises flag[rank] = e in every buffer
-// (after a system-scope fence). peer_merge_kernel waits until every flag has reached e (bounded),
+// rank's buffer (stores over NVLink), one CTA per destination, each raising flag[rank] = e in its
+// destination after a system-scope fence. peer_merge_kernel waits until every flag has reached e (bounded),
 // merges each row's world * nparts states in ascending (rank, part) order -- the order of the
 // single-GPU split plan -- and its last CTA records e as completed. A rank can be at most one call
 // ahead of another (its next push follows its own merge, which needs everyone's flag), so two
@@ -266,7 +266,7 @@ constexpr int64_t kPeerHeaderBytes = 256;
 constexpr long long kPeerWaitCycles = 1ll << 31;
 struct PeerHeader {
     unsigned int ep;          // epoch of the last completed exchange on this rank
-    unsigned int push_done;   // CTAs of the current push that have finished (reset by the last)
+    unsigned int unused;
     unsigned int merge_done;  // the same for the merge
     unsigned int pad;
     unsigned int flag[kMaxPeers];
@@ -276,32 +276,31 @@ struct PeerPtrs {
     unsigned char* p[kMaxPeers];  // every rank's exchange buffer as mapped in this process
 };
 
-__global__ void __launch_bounds__(256)
+// One CTA per destination rank: CTA r writes this rank's states into rank r's buffer, fences at
+// system scope and raises flag[rank] there, so each flag follows exactly the stores it announces.
+constexpr int kPushThreads = 512;
+__global__ void __launch_bounds__(kPushThreads)
 peer_push_kernel(const nb200_state* __restrict__ states, int64_t rows, int64_t nlocal, int64_t nparts,
                  PeerPtrs peers, int world, int rank, unsigned char* own) {
     pdl_wait();
     pdl_trigger();
-    PeerHeader* h = reinterpret_cast<PeerHeader*>(own);
-    const unsigned int e = *reinterpret_cast<volatile unsigned int*>(&h->ep) + 1u;
+    const PeerHeader* h = reinterpret_cast<const PeerHeader*>(own);
+    const unsigned int e = *reinterpret_cast<const volatile unsigned int*>(&h->ep) + 1u;
     const int64_t par = e & 1u, n = rows * nparts;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    unsigned char* dst = peers.p[blockIdx.x];
+    float4* slots = reinterpret_cast<float4*>(dst + kPeerHeaderBytes);
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
         const int64_t row = i / nparts, part = i - row * nparts;
         // parts past this rank's own count are empty states (unequal shard widths)
         const float4 v = part < nlocal ? reinterpret_cast<const float4*>(states)[row * nlocal + part]
                                        : make_float4(-NB200_INF, 0.f, 0.f, 0.f);
-        const int64_t slot = ((par * rows + row) * world + rank) * nparts + part;
-        for (int r = 0; r < world; ++r)
-            reinterpret_cast<float4*>(peers.p[r] + kPeerHeaderBytes)[slot] = v;
+        slots[((par * rows + row) * world + rank) * nparts + part] = v;
     }
     __threadfence_system();
     __syncthreads();
-    if (threadIdx.x == 0 && atomicAdd(&h->push_done, 1u) == gridDim.x - 1) {
-        atomicExch(&h->push_done, 0u);
-        __threadfence_system();
-        for (int r = 0; r < world; ++r) {
-            unsigned int* f = &reinterpret_cast<PeerHeader*>(peers.p[r])->flag[rank];
-            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
-        }
+    if (threadIdx.x == 0) {
+        unsigned int* f = &reinterpret_cast<PeerHeader*>(dst)->flag[rank];
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
     }
 }
 
@@ -659,8 +658,7 @@ int launch_peer_push(const nb200_state* states, int64_t rows, int64_t nlocal, in
                      int world, int rank, void* own, cudaStream_t st) {
     PeerPtrs pp{};
     for (int r = 0; r < world; ++r) pp.p[r] = static_cast<unsigned char*>(peers[r]);
-    const int g = persistent_grid(peer_push_kernel, 256, 0, (rows * nparts + 255) / 256, 0);
-    launch_pdl(peer_push_kernel, g, 256, 0, st, states, rows, nlocal, nparts, pp, world, rank,
+    launch_pdl(peer_push_kernel, world, kPushThreads, 0, st, states, rows, nlocal, nparts, pp, world, rank,
                static_cast<unsigned char*>(own));
     count_launch();
     return finish_launch("nb200_peer_push");

@@ -151,33 +151,51 @@ class PeerExchange:
         if nbytes < 0:
             raise ValueError(f"no peer exchange for rows={rows}, world={self.world}, nparts={nparts} (world <= 8)")
         device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-        self._storage = torch.zeros(nbytes + 256, dtype=torch.uint8, device=device)
-        pad = (-self._storage.data_ptr()) % 256
-        self.buffer = self._storage[pad:pad + nbytes]
-        handle = (ctypes.c_char * 64)()
-        offset = ctypes.c_int64()
-        _lib.check(lib.nb200_ipc_handle(ctypes.c_void_p(self.buffer.data_ptr()), handle, ctypes.byref(offset)),
-                   "peer exchange handle")
-        torch.cuda.synchronize(device)  # the buffer is zero before any peer can write into it
+        # Every collective below runs on every rank whatever happened locally, and every decision is
+        # taken from gathered results, so a failure on one rank raises on all of them together.
+        mine = None
+        try:
+            self._storage = torch.zeros(nbytes + 256, dtype=torch.uint8, device=device)
+            pad = (-self._storage.data_ptr()) % 256
+            self.buffer = self._storage[pad:pad + nbytes]
+            handle = (ctypes.c_char * 64)()
+            offset = ctypes.c_int64()
+            _lib.check(lib.nb200_ipc_handle(ctypes.c_void_p(self.buffer.data_ptr()), handle, ctypes.byref(offset)),
+                       "peer exchange handle")
+            torch.cuda.synchronize(device)  # the buffer is zero before any peer can write into it
+            mine = (bytes(handle), int(offset.value), self.rows, self.nparts)
+        except Exception as exc:  # noqa: BLE001 -- reported on every rank below
+            mine = ("error", f"rank {self.rank}: {exc}")
         everyone = [None] * self.world
-        td.all_gather_object(everyone, (bytes(handle), int(offset.value), self.rows, self.nparts), group=group)
+        td.all_gather_object(everyone, mine, group=group)
+        errors = [e[1] for e in everyone if e[0] == "error"]
+        if errors:
+            raise RuntimeError("peer exchange set-up failed: " + "; ".join(errors))
         # Every rank writes into every other rank's buffer at offsets computed from (rows, nparts):
-        # the layouts must agree before anything is mapped (all ranks see the same list and agree).
+        # the layouts must agree before anything is mapped.
         layouts = {(rows_r, parts_r) for _, _, rows_r, parts_r in everyone}
         if len(layouts) != 1:
             raise ValueError(f"ranks disagree on the exchange layout (rows, nparts): {sorted(layouts)}")
-        ptrs = []
-        try:
-            for r, (h, off, _, _) in enumerate(everyone):
-                if r == self.rank:
-                    ptrs.append(self.buffer.data_ptr())
-                    continue
-                base = ctypes.c_void_p()
-                _lib.check(lib.nb200_ipc_open(h, ctypes.byref(base)), f"peer exchange: map rank {r}")
-                self._opened.append(base.value)
-                ptrs.append(base.value + off)
-        finally:
-            td.barrier(group=group)  # every rank has mapped every buffer before the first push
+        ptrs, failure = [], None
+        for r, (h, off, _, _) in enumerate(everyone):
+            if r == self.rank:
+                ptrs.append(self.buffer.data_ptr())
+                continue
+            base = ctypes.c_void_p()
+            if lib.nb200_ipc_open(h, ctypes.byref(base)) != 0:
+                failure = f"rank {self.rank} cannot map rank {r}: {_lib.last_error()}"
+                break
+            self._opened.append(base.value)
+            ptrs.append(base.value + off)
+        failures = [None] * self.world
+        td.all_gather_object(failures, failure, group=group)
+        failures = [f for f in failures if f]
+        if failures:
+            for base in self._opened:
+                lib.nb200_ipc_close(ctypes.c_void_p(base))
+            self._opened = []
+            raise RuntimeError("peer exchange mapping failed: " + "; ".join(failures))
+        td.barrier(group=group)  # every rank has mapped every buffer before the first push
         self.peers = (ctypes.c_void_p * self.world)(*ptrs)
 
     def exchange_and_merge(self, name, params, states, out):
