@@ -311,25 +311,22 @@ peer_merge_kernel(unsigned char* own, T* __restrict__ out, int64_t rows, int64_t
     pdl_trigger();
     PeerHeader* h = reinterpret_cast<PeerHeader*>(own);
     const unsigned int e = *reinterpret_cast<volatile unsigned int*>(&h->ep) + 1u;
-    __shared__ int arrived;
-    if (threadIdx.x == 0) {
-        bool ok = true;
+    // Thread r waits for rank r's flag, so the ranks' system-scope polls overlap.
+    bool ok = true;
+    if (threadIdx.x < world) {
         const long long t0 = clock64();
-        for (int r = 0; r < world && ok; ++r) {
-            for (unsigned int it = 0;; ++it) {
-                unsigned int f;
-                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(&h->flag[r]) : "memory");
-                if ((int)(f - e) >= 0) break;
-                if ((it & 63u) == 63u && clock64() - t0 > kPeerWaitCycles) {
-                    ok = false;
-                    break;
-                }
+        for (unsigned int it = 0;; ++it) {
+            unsigned int f;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(&h->flag[threadIdx.x]) : "memory");
+            if ((int)(f - e) >= 0) break;
+            if ((it & 63u) == 63u && clock64() - t0 > kPeerWaitCycles) {
+                ok = false;
+                atomicOr(&g_peer_fault, 4u);
+                break;
             }
         }
-        if (!ok) atomicOr(&g_peer_fault, 4u);
-        arrived = ok;
     }
-    __syncthreads();
+    const bool arrived = __syncthreads_and(ok) != 0;
     if (arrived) {
         const int lane = threadIdx.x & 31;
         const int64_t total = (int64_t)world * nparts;
