@@ -641,6 +641,11 @@ def main():
                 "GB_per_s": round(r["bytes"] / (sms_ * 1e-3) / 1e9, 1),
                 "rows_per_s": round(r["rows"] / (sms_ * 1e-3), 1), "timing": how,
                 "algorithmic_bytes_per_step": r["bytes"], "launches_per_step": r["launches"]}
+            # a wait that ran out on any rank (fault bit) voids the region's timing on every rank
+            fault = torch.tensor([NB._lib.stream_fault()], dtype=torch.int64, device="cuda")
+            torch.distributed.all_reduce(fault, op=torch.distributed.ReduceOp.MAX)
+            if int(fault.item()):
+                regions[r["name"]] = {"workload": r["desc"], "fault": f"bounded wait ran out (bits {int(fault.item()):#x})"}
             if r["exchange"] is not None:
                 r["exchange"].close()
             del r
