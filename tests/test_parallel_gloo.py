@@ -157,6 +157,22 @@ def test_sharded_split_fold_exchange_branch_matches_all_gather():
         assert calls == 1 and refused
 
 
+def _peer_setup_worker(rank, world):
+    """PeerExchange set-up that fails locally (no GPU here): every rank must raise, none may hang."""
+    try:
+        parallel.PeerExchange(8, 2, device="cuda:0")
+    except RuntimeError as exc:
+        return "raised", str(exc)
+    return "constructed", ""
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the failure path of a machine without GPUs")
+def test_peer_exchange_setup_failure_raises_on_every_rank():
+    for outcome, message in _run(2, _peer_setup_worker):
+        assert outcome == "raised" and "set-up failed" in message
+        assert "rank 0" in message and "rank 1" in message  # each rank reports every rank's failure
+
+
 def _segment_worker(rank, world, T, nseg, channels):
     import oracle
 
