@@ -201,7 +201,7 @@ def make_rms(torch, NB, seed):
         NB.template.launch_rms_norm(xs[k], gamma, outs[k], eps=1e-6)
 
     return {"name": "rms_norm", "step": step, "bytes": rows * ncols * 2 * 2 + ncols * 2, "rows": rows,
-            "launches": 1, "buffers": nbuf,
+            "launches": 1, "buffers": nbuf, "io0": {"x": xs[0], "gamma": gamma, "y": outs[0]},
             "desc": f"rms_norm bf16 x[{rows},{ncols}] gamma[{ncols}] eps=1e-6 -> bf16 [{rows},{ncols}]"}
 
 
@@ -228,7 +228,7 @@ def make_softmax(torch, NB, seed):
         NB._lib.check(rc, "softmax")
 
     return {"name": "softmax_lse", "step": step, "bytes": rows * ncols * 4 * 2 + rows * 4, "rows": rows,
-            "launches": 1, "buffers": nbuf,
+            "launches": 1, "buffers": nbuf, "io0": {"x": xs[0], "y": ys[0], "lse": lse},
             "desc": f"softmax + logsumexp fp32 x[{rows},{ncols}] N(0,2^2), every 64th row +80 -> y[{rows},{ncols}], lse[{rows}]"}
 
 
@@ -249,7 +249,7 @@ def make_lse(torch, NB, seed):
         NB.template.launch_reduction("logsumexp", "serial", xs[k], out, rows, ncols, None, None, {"tiny": 0.0})
 
     return {"name": "logsumexp", "step": step, "bytes": rows * ncols * 4 + rows * 4, "rows": rows, "launches": 1,
-            "buffers": nbuf, "desc": f"logsumexp fp32 x[{rows},{ncols}] -> [{rows}]"}
+            "buffers": nbuf, "io0": {"x": xs[0], "out": out}, "desc": f"logsumexp fp32 x[{rows},{ncols}] -> [{rows}]"}
 
 
 def make_l2(torch, NB, seed):
@@ -271,7 +271,7 @@ def make_l2(torch, NB, seed):
         NB._lib.check(rc, "l2")
 
     return {"name": "l2_normalize", "step": step, "bytes": rows * ncols * 2 * 2 + rows * 2, "rows": rows,
-            "launches": 1, "buffers": nbuf, "desc": f"L2-normalize fp16 x[{rows},{ncols}] -> y, norm"}
+            "launches": 1, "buffers": nbuf, "io0": {"x": xs[0], "y": ys[0], "norm": norm}, "desc": f"L2-normalize fp16 x[{rows},{ncols}] -> y, norm"}
 
 
 def make_wide_lse(torch, NB, seed):
@@ -285,7 +285,7 @@ def make_wide_lse(torch, NB, seed):
         NB.template.launch_reduction("logsumexp", "split", xs[i % nbuf], out, rows, ncols, block, 8, {"tiny": 0.0})
 
     return {"name": "wide_logsumexp_split", "step": step, "bytes": rows * ncols * 2 + rows * 2, "rows": rows,
-            "launches": 2, "buffers": nbuf,
+            "launches": 2, "buffers": nbuf, "io0": {"x": xs[0], "out": out},
             "desc": f"logsumexp bf16 x[{rows},{ncols}] N(0,3^2), split plan {block}-column chunks -> [{rows}]"}
 
 
@@ -300,13 +300,14 @@ def make_segments(torch, NB, seed, reduce="sum"):
     from neptune_opt_b200.torch_op import _launch_segment
 
     params = {"initial": None, "offsets": True, "unsafe": False}
+    last = {}
 
     def step(i):
-        _launch_segment("segment_" + reduce, data, offsets, params, "serial")
+        last["out"] = _launch_segment("segment_" + reduce, data, offsets, params, "serial")
 
     return {"name": f"segment_{reduce}", "step": step,
             "bytes": T * channels * 2 + (nseg + 1) * 8 + nseg * channels * 2, "rows": nseg, "launches": 1,
-            "buffers": 1, "T": T,
+            "buffers": 1, "T": T, "io0": {"data": data, "offsets": offsets, "lengths": lengths, "last": last},
             "desc": f"ordered segment_{reduce} fp16 data[{T},{channels}], {nseg} segments Poisson(20) in [1,200], int64 offsets"}
 
 

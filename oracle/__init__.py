@@ -62,6 +62,7 @@ def lib():
         L.oracle_softmax.argtypes = [_int, _f32p, _i64, _i64, _f32p, _f32p]
         L.oracle_l2_normalize.argtypes = [_f32p, _i64, _i64, _int, _f32p, _f32p]
         L.oracle_rms_norm.argtypes = [_f32p, _f32p, _i64, _i64, ctypes.c_double, _int, _f32p]
+        L.oracle_rms_scale.argtypes = [_f32p, _i64, _i64, ctypes.c_double, _f32p]
         L.oracle_segment_spans.argtypes = [_i64p, _i64, _int, _int, _i64, _i64p]
         L.oracle_segment_spans.restype = ctypes.c_uint32
         L.oracle_segment_pool.argtypes = [_f32p, _i64, _i64, _i64p, _i64, _int, _int, ctypes.c_float, _int, _f32p]
@@ -148,6 +149,15 @@ def rms_norm(x, gamma, eps: float, dtype: str) -> np.ndarray:
     out = np.empty_like(x)
     lib().oracle_rms_norm(x, gamma, rows, ncols, float(eps), DTYPE_CODES[dtype], out)
     return out
+
+
+def rms_scale(x, eps: float) -> np.ndarray:
+    """Per-row fp32 scale rsqrt(mean(x^2) + eps) of the RMSNorm stages (binary64 sum, rounded once)."""
+    x = _f32(x)
+    rows, ncols = x.shape
+    scale = np.empty(rows, np.float32)
+    lib().oracle_rms_scale(x, rows, ncols, float(eps), scale)
+    return scale
 
 
 def segment_spans(segments, is_offsets: bool, unsafe: bool, nrows: int):

@@ -20,6 +20,7 @@
  *   oracle_softmax     log-family readout of the lowering, neptune_recognize/lowering.py:80-99
  *   oracle_l2_normalize stable_l2 fold (library.py:32-38) then x / norm
  *   oracle_rms_norm    RMSNorm numeric stages, emitters.py:576-595, skeleton.py:213-217
+ *   oracle_rms_scale   the per-row fp32 scale of those stages (emitters.py:576-586)
  *   oracle_segment_spans  torch_op.py:370-387 (cumsum + the four assertions, as status bits)
  *   oracle_segment_pool   torch_op.py:286-306 (ordered storage-dtype fold)
  */
@@ -255,6 +256,20 @@ static float rsqrt_rn(float v) {
     /* 1/sqrt in 64-bit-significand extended precision, rounded once to binary32. */
     long double r = 1.0L / sqrtl((long double)v);
     return (float)r;
+}
+
+/* Per-row fp32 scale rsqrt_rn(div_rn(total, count) + eps) of the RMSNorm stages (emitters.py:576-586),
+ * with the binary64-summed total rounded once to binary32. */
+void oracle_rms_scale(const float* x, int64_t rows, int64_t ncols, double eps, float* scale) {
+    const float count = (float)ncols, e = (float)eps;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+        const float* v = x + r * ncols;
+        double total_d = 0.0;
+        for (int64_t i = 0; i < ncols; ++i) total_d += (double)v[i] * v[i];
+        float total = (float)total_d;
+        scale[r] = rsqrt_rn(total / count + e);
+    }
 }
 
 void oracle_rms_norm(const float* x, const float* gamma, int64_t rows, int64_t ncols, double eps,
