@@ -8,18 +8,23 @@
 Headline workload (BASELINE.json configs[1]): RMSNorm bf16 x[16384, 4096], gamma[4096], eps 1e-6;
 one step = one fused RMSNorm pass over the batch. Every rank processes its own full batch (rows are
 independent, no data-path collective): weak scaling, `value` = all ranks' algorithmic bytes / the
-max-over-ranks step time. The other configs are measured after the headline and reported under
-`regions` (softmax+logsumexp fp32, L2-normalize fp16, split-plan logsumexp bf16, ordered segment
-sum/mean fp16, and the fused tcgen05 attention bf16 [8,32,4096,128] non-causal and causal in
-TFLOP/s against the measured bf16 tensor peak), each with its own roofline fraction.
+max-over-ranks step time. The other configs are measured after the headline and reported compactly
+under `roofline.regions` (ms per step, aggregate GB/s or TFLOP/s, the per-GPU fraction of the
+measured peak, ncu DRAM bytes per launch): softmax+logsumexp fp32, logsumexp fp32, L2-normalize
+fp16, split-plan logsumexp bf16, ordered segment sum/mean fp16, and the fused tcgen05 attention bf16
+[8,32,4096,128] non-causal and causal (burst and sustained, with torch SDPA on the same inputs as
+library context). With N > 1 GPUs the strong-scaled partitions follow: RMSNorm rows, segment
+blocks and attention heads of one fixed configuration, and the column-sharded split plan over NCCL
+and over NVLink peer memory. Workload descriptions go to stderr (`bench detail`).
 
 Algorithmic bytes count every tensor once (inputs read + outputs written). Between timed steps the
 inputs rotate over buffer sets whose total exceeds the 126 MB L2, so no step reads data a previous
 step left in L2. Times are CUDA events on the launching stream; the maximum over ranks is reported.
 
-`--impl reference` times the reference path's CPU implementation (the C restatement in oracle/,
-built from the reference's algorithm; the reference itself is pure Python/Triton and has no CPU
-kernel) on the same config with all host threads, over a bounded row sample per step.
+`--impl reference` times the reference's own CPU path for the headline: its unfused ATen RMSNorm
+graph (restated op for op in oracle/aten_graph.py and bit-identical to the reference's outputs) on
+torch's CPU kernels with all host threads, over the full batch per step. `cpu_baseline` reports the
+same path, with the C restatement's (oracle/oracle.c) figure beside it.
 """
 from __future__ import annotations
 
@@ -365,6 +370,99 @@ def make_sharded_split(torch, NB, seed, dist, peer=False):
                     f"{block}-column chunk states {how}, merged in rank order"}
 
 
+def make_rms_rows_sharded(torch, NB, seed, dist):
+    """BASELINE config 2 strong-scaled: the [16384, 4096] bf16 batch's rows split into one
+    contiguous block per rank (parallel.shard_rows); no data-path collective."""
+    from neptune_opt_b200.parallel import shard_rows
+
+    rows, ncols = 16384, 4096
+    b, e = shard_rows(rows, dist.world, dist.rank)
+    local = e - b
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    nbuf = max(2, -(-3 * L2_BYTES // (2 * local * ncols * 2)) + 1)
+    xs = [torch.randn(local, ncols, device="cuda", dtype=torch.bfloat16, generator=g) for _ in range(nbuf)]
+    outs = [torch.empty_like(xs[0]) for _ in range(nbuf)]
+    gamma = (1 + 0.1 * torch.randn(ncols, device="cuda", generator=g)).to(torch.bfloat16)
+
+    def step(i):
+        NB.template.launch_rms_norm(xs[i % nbuf], gamma, outs[i % nbuf], eps=1e-6)
+
+    return {"name": "rms_norm_rows_sharded", "step": step, "bytes": rows * ncols * 4 + ncols * 2, "rows": rows,
+            "launches": 1, "buffers": nbuf,
+            "desc": f"rms_norm bf16 [16384,4096], rows sharded over {dist.world} GPU(s) ({local} here)"}
+
+
+def make_segments_sharded(torch, NB, seed, dist, reduce="sum"):
+    """BASELINE config 4 strong-scaled: whole segments in contiguous blocks whose token counts
+    balance (parallel.shard_segments); each rank pools its block, bit-exact, no collective."""
+    from neptune_opt_b200.parallel import local_offsets, shard_segments
+    from neptune_opt_b200.torch_op import _launch_segment
+
+    nseg, channels = 200000, 128
+    gen = torch.Generator().manual_seed(0)
+    lengths = torch.poisson(torch.full((nseg,), 20.0), generator=gen).clamp(1, 200).to(torch.int64)
+    offsets = torch.cat([torch.zeros(1, dtype=torch.int64), lengths.cumsum(0)])
+    T = int(offsets[-1])
+    shard = shard_segments(offsets, dist.world, dist.rank)
+    local_off = local_offsets(offsets, shard).cuda()
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    data = torch.randn(shard.row_end - shard.row_begin, channels, device="cuda", dtype=torch.float16, generator=g)
+    params = {"initial": None, "offsets": True, "unsafe": False}
+
+    def step(i):
+        _launch_segment("segment_" + reduce, data, local_off, params, "serial")
+
+    return {"name": f"segment_{reduce}_sharded", "step": step,
+            "bytes": T * channels * 2 + (nseg + 1) * 8 + nseg * channels * 2, "rows": nseg, "launches": 1,
+            "buffers": 1,
+            "desc": f"segment_{reduce} fp16 [{T},128], 200000 segments in token-balanced blocks over "
+                    f"{dist.world} GPU(s) ({shard.seg_end - shard.seg_begin} here)"}
+
+
+def make_attention_sharded(torch, NB, seed, dist, causal=False):
+    """BASELINE config 5 strong-scaled: the 8 x 32 (batch, head) pairs split into contiguous blocks
+    (parallel.shard_heads), each rank running its block as one [1, pairs, 4096, 128] launch."""
+    from neptune_opt_b200.attention import launch_attention
+    from neptune_opt_b200.parallel import shard_heads
+
+    b, h, s, d = 8, 32, 4096, 128
+    lo, hi = shard_heads(b, h, dist.world, dist.rank)
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q, k, v = (torch.randn(1, hi - lo, s, d, device="cuda", dtype=torch.bfloat16, generator=g) for _ in range(3))
+    o = torch.empty_like(q)
+    lse = torch.empty(1, hi - lo, s, device="cuda", dtype=torch.float32)
+
+    def step(_i):
+        launch_attention(q, k, v, o, lse, causal=causal, scale=1.0 / d ** 0.5)
+
+    pairs = s * s if not causal else s * (s + 1) // 2
+    return {"name": "attention" + ("_causal" if causal else "") + "_heads_sharded", "step": step,
+            "flops": 4 * b * h * d * pairs, "rows": b * h * s, "launches": 1, "buffers": 1,
+            "desc": f"attention bf16 [8,32,4096,128]{' causal' if causal else ''}, (batch, head) pairs sharded "
+                    f"over {dist.world} GPU(s) ({hi - lo} here)"}
+
+
+def sdpa_tflops(torch, causal, flops):
+    """torch's scaled_dot_product_attention (library kernels) on the same [8,32,4096,128] bf16
+    inputs, 10 launches between CUDA events: context for the attention regions."""
+    import torch.nn.functional as F
+
+    g = torch.Generator(device="cuda").manual_seed(7)
+    q, k, v = (torch.randn(8, 32, 4096, 128, device="cuda", dtype=torch.bfloat16, generator=g) for _ in range(3))
+    for _ in range(3):
+        F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(10):
+        F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / 10
+    del q, k, v
+    return round(flops / (ms * 1e-3) / 1e12, 1)
+
+
 def gpu_id(torch) -> str:
     """nvidia-smi id of the current device (PCI bus id when torch exposes it)."""
     props = torch.cuda.get_device_properties(torch.cuda.current_device())
@@ -476,65 +574,114 @@ def roofline(bytes_per_launch, ms, peaks, traffic):
             "traffic": traffic}
 
 
-# ---------------------------------------------------------------- CPU baseline (oracle port)
-def cpu_rms_sample(seconds: float):
-    """The oracle's RMSNorm (the reference algorithm restated in C, all host threads) over the
-    headline batch, repeated for about `seconds`."""
+# ---------------------------------------------------------------- CPU legs (reference path on the host)
+def _host_rms_inputs(rows, ncols, seed=0):
+    """Seeded host copies of the headline inputs: x bf16 ~ N(0,1), gamma bf16 ~ N(1, 0.1)."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(rows, ncols, generator=g).to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(ncols, generator=g)).to(torch.bfloat16)
+    return x, gamma
+
+
+def _host_threads():
+    """Use every host core for the CPU legs; returns the thread count torch will use."""
+    import torch
+
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    return torch.get_num_threads()
+
+
+def time_aten_rms(steps: int, warmup: int, budget_s: float):
+    """The reference's unfused ATen RMSNorm graph (oracle/aten_graph.py, bit-identical to the
+    reference's outputs) on the host: (seconds per step, rows per step, threads). Each step is the
+    full [16384, 4096] batch unless `steps` full passes would exceed `budget_s`, in which case each
+    step is a leading row block sized to fit (declared by the caller)."""
+    import time as _t
+
+    from oracle import aten_graph
+
+    threads = _host_threads()
+    rows, ncols = 16384, 4096
+    x, gamma = _host_rms_inputs(rows, ncols)
+    t0 = _t.perf_counter()
+    aten_graph.rms_norm(x, gamma, 1e-6)
+    first = _t.perf_counter() - t0
+    sample = rows
+    if first * (steps + warmup) > budget_s:
+        sample = max(256, int(rows * budget_s / (first * (steps + warmup))) // 256 * 256)
+    xs = x[:sample]
+    for _ in range(max(0, warmup - 1)):
+        aten_graph.rms_norm(xs, gamma, 1e-6)
+    t0 = _t.perf_counter()
+    for _ in range(steps):
+        aten_graph.rms_norm(xs, gamma, 1e-6)
+    return (_t.perf_counter() - t0) / steps, sample, threads
+
+
+def time_c_port_rms(seconds: float):
+    """The C restatement (oracle/oracle.c, OpenMP over all host threads) over the full headline
+    batch, repeated for about `seconds`: (GB/s at bf16 bytes, threads, passes)."""
     import numpy as np
 
     import oracle
 
     rows, ncols = 16384, 4096
-    rng = np.random.default_rng(0)
-    x = rng.standard_normal((rows, ncols), dtype=np.float32)
-    gamma = (1 + 0.1 * rng.standard_normal(ncols)).astype(np.float32)
-    oracle.rms_norm(x[:64], gamma, 1e-6, "bfloat16")  # load + warm
+    x, gamma = _host_rms_inputs(rows, ncols)
+    xf, gf = x.float().numpy(), gamma.float().numpy()
+    oracle.rms_norm(xf[:64], gf, 1e-6, "bfloat16")  # load + warm
     t0 = time.perf_counter()
     reps = 0
     while True:
-        oracle.rms_norm(x, gamma, 1e-6, "bfloat16")
+        oracle.rms_norm(xf, gf, 1e-6, "bfloat16")
         reps += 1
         if time.perf_counter() - t0 >= seconds:
             break
     dt = time.perf_counter() - t0
-    nbytes = reps * (rows * ncols * 2 * 2 + ncols * 2)
-    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": oracle.num_threads(), "kind": "port",
-            "sample": f"{reps} full passes over x[{rows},{ncols}] in {dt:.1f} s (fp32 host copy of the bf16 "
-                      f"values; bytes counted at bf16), rows/s={reps * rows / dt:.0f}"}
+    del np
+    return reps * (rows * ncols * 4 + ncols * 2) / dt / 1e9, oracle.num_threads(), reps
+
+
+RMS_BYTES_PER_ROW = 4096 * 2 * 2  # read x + write y, bf16
+ATEN_PATH = ("the reference's unfused ATen RMSNorm graph on the host (tests/test_recognize.py:595-597 form, "
+             "oracle/aten_graph.py, bit-identical to the reference's outputs), torch CPU kernels")
+
+
+def cpu_baseline_rms(seconds: float):
+    """cpu_baseline of the headline: the reference's ATen graph on host cores, with the C port's
+    figure beside it."""
+    steps = 8
+    dt, sample, threads = time_aten_rms(steps, 1, seconds)
+    value = sample * RMS_BYTES_PER_ROW / dt / 1e9
+    cport, cthreads, reps = time_c_port_rms(min(5.0, seconds / 2))
+    return {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{steps} passes of {sample} of the 16384 rows (x bf16 [.,4096], gamma bf16) through "
+                      f"{ATEN_PATH}; {dt * 1e3:.0f} ms per pass",
+            "c_port_GBps": round(cport, 3),
+            "c_port": f"oracle/oracle.c restatement, {cthreads} OpenMP threads, {reps} full passes"}
 
 
 def run_reference(args):
-    """`--impl reference`: the CPU path on rank 0 only."""
+    """`--impl reference`: the reference's CPU path for the headline on rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    import numpy as np
-
-    import oracle
-
-    rows_sample, ncols = 2048, 4096
-    rng = np.random.default_rng(0)
-    x = rng.standard_normal((rows_sample, ncols), dtype=np.float32)
-    gamma = (1 + 0.1 * rng.standard_normal(ncols)).astype(np.float32)
-    for _ in range(args.warmup):
-        oracle.rms_norm(x, gamma, 1e-6, "bfloat16")
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        oracle.rms_norm(x, gamma, 1e-6, "bfloat16")
-    dt = (time.perf_counter() - t0) / args.steps
-    nbytes = rows_sample * ncols * 2 * 2 + ncols * 2
-    value = nbytes / dt / 1e9
-    sample = f"{rows_sample} of the 16384 rows per step (fp32 host copy of bf16 values; bytes counted at bf16)"
+    dt, sample, threads = time_aten_rms(args.steps, args.warmup, 150.0)
+    value = sample * RMS_BYTES_PER_ROW / dt / 1e9
+    full = sample == 16384
+    desc = ("full batch" if full else f"leading {sample} of the 16384 rows (the full batch per step would "
+            f"exceed the time budget)")
     line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "impl": "reference",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 4),
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) x, N(1,0.1) gamma)",
-            "config": {"workload": "rms_norm bf16 x[16384,4096] gamma[4096] eps=1e-6 (row sample per step)",
-                       "rows_per_step": rows_sample, "ncols": ncols},
-            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": oracle.num_threads(),
-                             "kind": "port", "sample": sample},
+            "config": {"workload": "rms_norm bf16 x[16384,4096] gamma[4096] eps=1e-6 -> bf16 [16384,4096]",
+                       "rows_per_step": sample, "ncols": 4096, "path": ATEN_PATH},
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": f"{desc} per step, {args.steps} timed steps after {args.warmup} warm-up"},
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "rows_per_s": round(rows_sample / dt, 1)}
+            "rows_per_s": round(sample / dt, 1)}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -568,6 +715,34 @@ def run_region(args, torch, NB, dist, peaks):
 
 
 # ---------------------------------------------------------------- main
+def hbm_region(r, ms, n, peaks, strong=False):
+    """Compact record of an HBM-bound region: ms per step (max over ranks), aggregate GB/s, the
+    per-GPU fraction of the measured copy peak, and ncu DRAM bytes per launch (profiles/)."""
+    per_gpu = r["bytes"] / (n if strong else 1)
+    rec = {"ms": round(ms, 5), "GBps": round((1 if strong else n) * r["bytes"] / (ms * 1e-3) / 1e9, 1),
+           "frac": round(per_gpu / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+           "traffic": profile_traffic(r["name"]) if n == 1 else None}
+    if strong:
+        rec["strong"] = True
+    return rec
+
+
+def tensor_region(r, ms, n, peaks, strong=False, sustained_ms=None, sdpa=None):
+    per_gpu = r["flops"] / (n if strong else 1)
+    rec = {"ms": round(ms, 5), "TFLOPs": round((1 if strong else n) * r["flops"] / (ms * 1e-3) / 1e12, 1),
+           "frac": round(per_gpu / (ms * 1e-3) / 1e12 / peaks["bf16_tflops"], 4),
+           "traffic": profile_traffic(r["name"]) if n == 1 else None}
+    if sustained_ms is not None:
+        sus = per_gpu / (sustained_ms * 1e-3) / 1e12
+        rec["sus_TFLOPs"] = round(sus * (1 if strong else n), 1)
+        rec["sus_frac"] = round(sus / peaks["bf16_tflops_sustained"], 4)
+    if sdpa is not None:
+        rec["sdpa_TFLOPs"] = sdpa
+    if strong:
+        rec["strong"] = True
+    return rec
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
@@ -583,13 +758,17 @@ def main():
     peaks = load_peaks()
     n = dist.world
     sampler = ClockSampler(gpu_id(torch)).start() if dist.rank == 0 else None
+    detail = {}
 
-    # ---- headline: RMSNorm
+    # ---- headline: RMSNorm, every rank its own [16384, 4096] batch (weak scaling)
     w = make_rms(torch, NB, seed=1000 + dist.rank)
     ms, launches = time_steps(torch, dist, w["step"], args.steps, max(3, args.warmup))
     eager_ms, _ = time_steps(torch, dist, w["step"], args.steps, max(3, args.warmup), graph=False)
     value = n * w["bytes"] / (ms * 1e-3) / 1e9
     head_roof = roofline(w["bytes"] / w["launches"], ms / w["launches"], peaks, profile_traffic("rms_norm"))
+    detail["rms_norm"] = {"workload": w["desc"], "eager_ms_per_step": round(eager_ms, 5)}
+    del w
+    torch.cuda.empty_cache()
 
     # ---- e2e through the public API with host buffers
     rows, ncols = 16384, 4096
@@ -604,51 +783,25 @@ def main():
 
     e2e_steps = max(3, min(args.steps, 30))
     e2e_ms, _ = time_steps(torch, dist, e2e_step, e2e_steps, 3, graph=False)
-    e2e = {"value": round(n * w["bytes"] / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+    e2e = {"value": round(n * (rows * ncols * 4 + ncols * 2) / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
            "h2d_bytes_per_step": rows * ncols * 2 + ncols * 2, "d2h_bytes_per_step": rows * ncols * 2,
            "ms_per_step": round(e2e_ms, 4), "steps": e2e_steps,
-           "path": "pinned host x,gamma -> neptune_opt_b200.run_rms_norm_host (nb200_rms_norm_host: 16 MiB "
-                   "row chunks, H2D / kernel / D2H overlapped on three streams) -> pinned host y"}
+           "path": "pinned host x,gamma -> run_rms_norm_host (nb200_rms_norm_host, 16 MiB chunks, copies "
+                   "overlapping the kernel) -> pinned host y"}
     del xh, gh, oh
 
-    # ---- the other fused regions
+    # ---- the other configurations
     regions = {}
     if not args.no_regions:
-        for maker in (make_softmax, make_lse, make_l2, make_wide_lse,
-                      lambda t, nb, s: make_segments(t, nb, s, "sum"),
-                      lambda t, nb, s: make_segments(t, nb, s, "mean")):
+        makers = [make_softmax, make_lse, make_l2, make_wide_lse,
+                  lambda t, nb, s: make_segments(t, nb, s, "sum"), lambda t, nb, s: make_segments(t, nb, s, "mean")]
+        for maker in makers:
             r = maker(torch, NB, 2000 + dist.rank)
             rms_, _ = time_steps(torch, dist, r["step"], args.steps, max(3, args.warmup))
-            eager_, _ = time_steps(torch, dist, r["step"], args.steps, max(3, args.warmup), graph=False)
-            regions[r["name"]] = {
-                "workload": r["desc"], "ms_per_step": round(rms_, 5), "eager_ms_per_step": round(eager_, 5),
-                "GB_per_s": round(n * r["bytes"] / (rms_ * 1e-3) / 1e9, 1),
-                "rows_per_s": round(n * r["rows"] / (rms_ * 1e-3), 1),
-                "pct_of_8TBs": round(100 * r["bytes"] / (rms_ * 1e-3) / 1e9 / NOMINAL_HBM_GBS, 2),
-                "roofline_frac_of_measured": round(r["bytes"] / (rms_ * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
-                "algorithmic_bytes_per_step": r["bytes"], "launches_per_step": r["launches"],
-                "traffic_bytes_per_launch": profile_traffic(r["name"]),
-                "l2_rotation_buffers": r["buffers"]}
-            del r
-            torch.cuda.empty_cache()
-        for peer in ((False, True) if n > 1 else ()):
-            r = make_sharded_split(torch, NB, 2600, dist, peer=peer)
-            if r is None:
-                continue
-            steps = min(args.steps, 50)
-            sms_, how = time_collective_steps(torch, dist, r["step"], steps, max(3, args.warmup))
-            regions[r["name"]] = {
-                "workload": r["desc"], "ms_per_step": round(sms_, 5), "scaling": "strong",
-                "GB_per_s": round(r["bytes"] / (sms_ * 1e-3) / 1e9, 1),
-                "rows_per_s": round(r["rows"] / (sms_ * 1e-3), 1), "timing": how,
-                "algorithmic_bytes_per_step": r["bytes"], "launches_per_step": r["launches"]}
-            # a wait that ran out on any rank (fault bit) voids the region's timing on every rank
-            fault = torch.tensor([NB._lib.stream_fault()], dtype=torch.int64, device="cuda")
-            torch.distributed.all_reduce(fault, op=torch.distributed.ReduceOp.MAX)
-            if int(fault.item()):
-                regions[r["name"]] = {"workload": r["desc"], "fault": f"bounded wait ran out (bits {int(fault.item()):#x})"}
-            if r["exchange"] is not None:
-                r["exchange"].close()
+            regions[r["name"]] = hbm_region(r, rms_, n, peaks)
+            detail[r["name"]] = {"workload": r["desc"], "launches_per_step": r["launches"],
+                                 "l2_rotation_buffers": r["buffers"],
+                                 "rows_per_s": round(n * r["rows"] / (rms_ * 1e-3), 1)}
             del r
             torch.cuda.empty_cache()
         for causal in (False, True):
@@ -657,47 +810,65 @@ def main():
             r = make_attention(torch, NB, 2500 + dist.rank, causal=causal)
             ams, _ = time_steps(torch, dist, r["step"], 10, max(3, args.warmup))
             sms, _ = time_steps(torch, dist, r["step"], 100, 3)
-            sus = tensor_roofline(r["flops"], sms, peaks, None)
-            sus["peak"] = peaks["bf16_tflops_sustained"]
-            sus["frac"] = round(sus["achieved"] / sus["peak"], 4)
-            sus["peak_source"] = peaks["source"] + " (sustained cuBLAS bf16 GEMM under the power cap)"
-            regions[r["name"]] = {
-                "workload": r["desc"], "ms_per_step": round(ams, 5), "steps": 10,
-                "TFLOP_per_s": round(n * r["flops"] / (ams * 1e-3) / 1e12, 1),
-                "rows_per_s": round(n * r["rows"] / (ams * 1e-3), 1),
-                "flops_per_step": r["flops"],
-                "roofline": tensor_roofline(r["flops"], ams, peaks, profile_traffic(r["name"])),
-                "sustained": {"steps": 100, "ms_per_step": round(sms, 5),
-                              "TFLOP_per_s": round(n * r["flops"] / (sms * 1e-3) / 1e12, 1), "roofline": sus},
-                "parallelism": f"heads: each of {n} GPU(s) runs its own [8,32,4096,128] batch"}
+            sdpa = sdpa_tflops(torch, causal, r["flops"]) if dist.rank == 0 else None
+            regions[r["name"]] = tensor_region(r, ams, n, peaks, sustained_ms=sms, sdpa=sdpa)
+            detail[r["name"]] = {"workload": r["desc"]}
             del r
             torch.cuda.empty_cache()
+        if n > 1:
+            # strong scaling: one fixed BASELINE configuration partitioned over the ranks
+            for maker, kind in ((make_rms_rows_sharded, "hbm"),
+                                (lambda t, nb, s, d: make_segments_sharded(t, nb, s, d, "sum"), "hbm"),
+                                (lambda t, nb, s, d: make_attention_sharded(t, nb, s, d, False), "tensor"),
+                                (lambda t, nb, s, d: make_attention_sharded(t, nb, s, d, True), "tensor")):
+                r = maker(torch, NB, 2700 + dist.rank, dist)
+                steps = args.steps if kind == "hbm" else 10
+                sms_, _ = time_steps(torch, dist, r["step"], steps, max(3, args.warmup))
+                regions[r["name"]] = (hbm_region(r, sms_, n, peaks, strong=True) if kind == "hbm"
+                                      else tensor_region(r, sms_, n, peaks, strong=True))
+                detail[r["name"]] = {"workload": r["desc"]}
+                del r
+                torch.cuda.empty_cache()
+            for peer in (False, True):
+                r = make_sharded_split(torch, NB, 2600, dist, peer=peer)
+                if r is None:
+                    continue
+                steps = min(args.steps, 50)
+                sms_, how = time_collective_steps(torch, dist, r["step"], steps, max(3, args.warmup))
+                rec = hbm_region(r, sms_, n, peaks, strong=True)
+                # a wait that ran out on any rank (fault bit) voids the region's timing on every rank
+                fault = torch.tensor([NB._lib.stream_fault()], dtype=torch.int64, device="cuda")
+                torch.distributed.all_reduce(fault, op=torch.distributed.ReduceOp.MAX)
+                if int(fault.item()):
+                    rec = {"fault": f"bounded wait ran out (bits {int(fault.item()):#x})"}
+                regions[r["name"]] = rec
+                detail[r["name"]] = {"workload": r["desc"], "timing": how}
+                if r["exchange"] is not None:
+                    r["exchange"].close()
+                del r
+                torch.cuda.empty_cache()
     clocks = sampler.stop() if sampler else None
 
     cpu = None
     if dist.rank == 0 and n == 1 and not args.no_cpu:
         try:
-            cpu = cpu_rms_sample(10.0)
+            cpu = cpu_baseline_rms(20.0)
         except Exception as exc:  # noqa: BLE001 -- the baseline is reported, never the measured value
             cpu = {"value": None, "unit": "GB/s", "cores": None, "kind": "port", "sample": f"failed: {exc}"}
 
     if dist.rank == 0:
+        head_roof["regions"] = regions
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": n, "steps": args.steps,
             "warmup": max(3, args.warmup), "ms_per_step": round(ms, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) x, N(1,0.1) gamma on device)",
-            "config": {"workload": w["desc"], "rows_per_gpu": 16384, "ncols": 4096,
-                       "timing": "K steps captured in one CUDA graph, replayed once between CUDA events "
-                                 "(device time; eager_ms_per_step times the same K steps launched from Python)",
-                       "parallelism": f"rows: each of {n} GPU(s) normalizes its own [16384,4096] block",
-                       "l2": f"inputs rotate over {w['buffers']} buffer pairs ({w['buffers'] * 2 * 128} MiB) > 126 MB L2"},
-            "eager_ms_per_step": round(eager_ms, 5),
-            "rows_per_s": round(n * w["rows"] / (ms * 1e-3), 1),
-            "pct_of_8TBs": round(100 * w["bytes"] / (ms * 1e-3) / 1e9 / NOMINAL_HBM_GBS, 2),
-            "roofline": head_roof, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": launches, "clocks": clocks, "regions": regions,
+            "config": {"workload": "rms_norm bf16 x[16384,4096] gamma[4096] eps=1e-6, per GPU",
+                       "timing": "K steps in one CUDA graph replay between CUDA events, max over ranks",
+                       "l2": "inputs rotate over buffers > 3x the 126 MB L2"},
+            "roofline": head_roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
         }
+        print("bench detail " + json.dumps(detail), file=sys.stderr, flush=True)
         print(json.dumps(line), flush=True)
     dist.close()
     return 0

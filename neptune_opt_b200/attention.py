@@ -75,21 +75,18 @@ _OP = None
 
 
 def attention_op():
-    """torch custom op `neptune_b200::attention(q, k, v, causal, scale) -> (O, LSE)` with a fake
-    (shape-only) implementation, so a graph holding it exports like the other region ops."""
+    """Op `neptune_b200::attention(q, k, v, causal, scale) -> (O, LSE)`. Like the region ops, its one
+    kernel is a composite body that checks the contract and calls the C++-registered
+    `nb200::attention`, so a graph holding it exports, and AOTInductor packages it as a call of the
+    C++ op."""
     global _OP
     if _OP is not None:
         return _OP
-    import torch
+    from neptune_opt_b200.torch_op import _nb200, _register
 
-    @torch.library.custom_op(OP_NAME, mutates_args=(),
-                             schema="(Tensor q, Tensor k, Tensor v, bool causal, float scale) -> (Tensor, Tensor)")
-    def _attention(q, k, v, causal, scale):
-        return run_attention(q, k, v, causal=causal, scale=scale, return_lse=True)
+    def _body(q, k, v, causal, scale):
+        sc = validate_attention_inputs(q, k, v, scale)
+        return tuple(_nb200().attention(q, k, v, causal, sc))
 
-    @_attention.register_fake
-    def _(q, k, v, causal, scale):
-        return torch.empty_like(q), q.new_empty(q.shape[:-1], dtype=torch.float32)
-
-    _OP = torch.ops.neptune_b200.attention.default
+    _OP = _register(OP_NAME, "(Tensor q, Tensor k, Tensor v, bool causal, float scale) -> (Tensor, Tensor)", _body)
     return _OP

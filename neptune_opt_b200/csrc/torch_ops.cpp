@@ -5,14 +5,19 @@
 // C++ kernel that calls the C ABI of libneptune_b200.so (include/neptune_b200.h).
 //
 // Ops (CUDA kernels + Meta kernels that compute shapes only, for export and fake tensors):
-//   fold(Tensor x, int skeleton, float[] params, bool keepdim, int plan, int block) -> Tensor
-//       params = [tiny, alpha, T, beta, N, eps]; plan 0 serial, 1 split (block-column chunks)
+//   fold(Tensor x, int skeleton, float[] params, bool keepdim, int plan, int block,
+//        int num_warps=0) -> Tensor
+//       params = [tiny, alpha, T, beta, N, eps]; plan 0 serial, 1 split (block-column chunks);
+//       serial launch from num_warps as the host launch policy maps (block, num_warps): 0 the
+//       library's own choice, 1 one warp per row, n > 1 one CTA of 32 n threads per row
 //   softmax(Tensor x, int mode) -> (Tensor y, Tensor lse)           mode 0 softmax, 1 log_softmax
 //   l2_normalize(Tensor x) -> (Tensor y, Tensor norm)
 //   rms_norm(Tensor x, Tensor gamma, float eps) -> Tensor
 //   segment_pool(Tensor data, Tensor segments, bool offsets, int reduce, float? initial,
 //                bool unsafe) -> Tensor                              reduce 0 sum, 1 mean
 //   segment_status(int device, bool clear) -> int
+//   segment_status_word(int device) -> Tensor      the per-device int32 word itself, for launches
+//                                                  made through the C ABI by other host code
 //   attention(Tensor q, Tensor k, Tensor v, bool causal, float scale) -> (Tensor o, Tensor lse)
 //
 // libneptune_b200.so is opened at the first call from the directory this library lives in, so
@@ -127,8 +132,20 @@ void check_cuda(const at::Tensor& t, const char* what) {
 }
 
 // ------------------------------------------------------------------ CUDA kernels
+// The launch a (block, num_warps) pair selects for the serial plan (nullptr: library default).
+const nb200_launch* serial_launch(int64_t num_warps, nb200_launch* storage) {
+    if (num_warps <= 0) return nullptr;
+    if (num_warps == 1) {
+        *storage = nb200_launch{NB200_VARIANT_WARP_ROW, 0, 0, 0};
+    } else {
+        TORCH_CHECK_VALUE(num_warps <= 16, "nb200.fold: num_warps must be in 0..16, got ", num_warps);
+        *storage = nb200_launch{NB200_VARIANT_CTA_ROW, (int32_t)(32 * num_warps), 0, 0};
+    }
+    return storage;
+}
+
 at::Tensor fold_cuda(const at::Tensor& x, int64_t skeleton, at::ArrayRef<double> params, bool keepdim, int64_t plan,
-                     int64_t block) {
+                     int64_t block, int64_t num_warps) {
     check_cuda(x, "nb200.fold");
     const int dt = dtype_code(x);
     c10::cuda::CUDAGuard guard(x.device());
@@ -137,8 +154,9 @@ at::Tensor fold_cuda(const at::Tensor& x, int64_t skeleton, at::ArrayRef<double>
     if (out.numel() == 0) return out;
     const at::Tensor x2 = rows_view(x);
     if (plan == 0) {
+        nb200_launch storage;
         check(api().fold((int)skeleton, &p, x2.data_ptr(), dt, x2.size(0), x2.size(1), x2.stride(0), x2.stride(1),
-                         out.data_ptr(), nullptr, stream_of(x)),
+                         out.data_ptr(), serial_launch(num_warps, &storage), stream_of(x)),
               "nb200.fold");
     } else {
         const int64_t chunk = block > 0 ? block : 16384;
@@ -264,6 +282,8 @@ at::Tensor segment_cuda(const at::Tensor& data, const at::Tensor& segments, bool
     return out;
 }
 
+at::Tensor segment_status_word(int64_t device) { return status_word(at::Device(at::kCUDA, (c10::DeviceIndex)device)); }
+
 int64_t segment_status(int64_t device, bool clear) {
     at::Tensor w = status_word(at::Device(at::kCUDA, (c10::DeviceIndex)device));
     const int64_t bits = w.item<int32_t>();
@@ -291,37 +311,49 @@ std::tuple<at::Tensor, at::Tensor> attention_cuda(const at::Tensor& q, const at:
 }
 
 // ------------------------------------------------------------------ Meta kernels (shapes only)
-at::Tensor fold_meta(const at::Tensor& x, int64_t, at::ArrayRef<double>, bool keepdim, int64_t, int64_t) {
-    return at::empty(lead_shape(x, keepdim), x.options());
+// Symbolic sizes throughout, so graphs exported with dynamic dimensions trace through these ops.
+std::vector<c10::SymInt> lead_sym_shape(const at::Tensor& x, bool keepdim) {
+    const auto s = x.sym_sizes();
+    std::vector<c10::SymInt> v(s.begin(), s.end() - 1);
+    if (keepdim) v.emplace_back(1);
+    return v;
+}
+at::Tensor fold_meta(const at::Tensor& x, int64_t, at::ArrayRef<double>, bool keepdim, int64_t, int64_t, int64_t) {
+    return at::empty_symint(lead_sym_shape(x, keepdim), x.options());
 }
 std::tuple<at::Tensor, at::Tensor> softmax_meta(const at::Tensor& x, int64_t) {
-    return {at::empty(x.sizes(), x.options()), at::empty(lead_shape(x, false), x.options())};
+    return {at::empty_symint(x.sym_sizes(), x.options()), at::empty_symint(lead_sym_shape(x, false), x.options())};
 }
 std::tuple<at::Tensor, at::Tensor> l2_meta(const at::Tensor& x) {
-    return {at::empty(x.sizes(), x.options()), at::empty(lead_shape(x, false), x.options())};
+    return {at::empty_symint(x.sym_sizes(), x.options()), at::empty_symint(lead_sym_shape(x, false), x.options())};
 }
-at::Tensor rms_meta(const at::Tensor& x, const at::Tensor&, double) { return at::empty(x.sizes(), x.options()); }
+at::Tensor rms_meta(const at::Tensor& x, const at::Tensor&, double) {
+    return at::empty_symint(x.sym_sizes(), x.options());
+}
 at::Tensor segment_meta(const at::Tensor& data, const at::Tensor& segments, bool offsets, int64_t,
                         std::optional<double>, bool) {
-    std::vector<int64_t> shape{offsets ? segments.size(0) - 1 : segments.size(0)};
-    for (int64_t d = 1; d < data.dim(); ++d) shape.push_back(data.size(d));
-    return at::empty(shape, data.options());
+    std::vector<c10::SymInt> shape{offsets ? segments.sym_size(0) - 1 : segments.sym_size(0)};
+    const auto ds = data.sym_sizes();
+    for (size_t d = 1; d < ds.size(); ++d) shape.push_back(ds[d]);
+    return at::empty_symint(shape, data.options());
 }
 std::tuple<at::Tensor, at::Tensor> attention_meta(const at::Tensor& q, const at::Tensor&, const at::Tensor&, bool,
                                                   double) {
-    return {at::empty(q.sizes(), q.options()),
-            at::empty({q.size(0), q.size(1), q.size(2)}, q.options().dtype(at::kFloat))};
+    const auto qs = q.sym_sizes();
+    return {at::empty_symint(qs, q.options()),
+            at::empty_symint(std::vector<c10::SymInt>(qs.begin(), qs.end() - 1), q.options().dtype(at::kFloat))};
 }
 
 }  // namespace
 
 TORCH_LIBRARY(nb200, m) {
-    m.def("fold(Tensor x, int skeleton, float[] params, bool keepdim, int plan, int block) -> Tensor");
+    m.def("fold(Tensor x, int skeleton, float[] params, bool keepdim, int plan, int block, int num_warps=0) -> Tensor");
     m.def("softmax(Tensor x, int mode) -> (Tensor, Tensor)");
     m.def("l2_normalize(Tensor x) -> (Tensor, Tensor)");
     m.def("rms_norm(Tensor x, Tensor gamma, float eps) -> Tensor");
     m.def("segment_pool(Tensor data, Tensor segments, bool offsets, int reduce, float? initial, bool unsafe) -> Tensor");
     m.def("segment_status(int device, bool clear) -> int", &segment_status);
+    m.def("segment_status_word(int device) -> Tensor", &segment_status_word);
     m.def("attention(Tensor q, Tensor k, Tensor v, bool causal, float scale) -> (Tensor, Tensor)");
 }
 

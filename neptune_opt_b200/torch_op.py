@@ -4,18 +4,29 @@ Mirrors neptune_codegen/torch_op.py: `as_cuda_op`/`op_handle` register one op pe
 parameters, keepdim, launch configuration, plan) with schema `(Tensor x) -> Tensor`;
 `as_state_op`/`state_op_handle` register the structured RMSNorm op `(Tensor x, Tensor gamma) ->
 Tensor` and dispatch segment pooling to `as_segment_op`/`segment_op_handle` with schema
-`(Tensor data, Tensor segments) -> Tensor`. Every handle is a `torch._ops.OpOverload` whose Fake
-implementation computes metadata only; the real implementation allocates a fresh output with torch
-and launches through the C ABI on the current stream.
+`(Tensor data, Tensor segments) -> Tensor`. Every handle is a `torch._ops.OpOverload` whose
+fake/meta evaluation computes metadata only.
+
+How a per-key op runs. Its only kernel is a CompositeImplicitAutograd body: it checks the
+reference's input contract, then calls the generic C++-registered region op of
+libneptune_b200_torch.so (`torch.ops.nb200.fold / rms_norm / segment_pool / softmax`) with the
+key's skeleton, parameters, plan and launch baked in as arguments. So
+* eager calls run the kernels through that C++ op (which calls the C ABI on the current stream);
+* a graph rewritten by the reference (neptune_recognize/rewrite.py:159-217) holds the per-key
+  node, which exports, saves and loads like any op;
+* when AOTInductor compiles such a graph (neptune_opt/ab.py:145-172), tracing replaces the per-key
+  node by its body, so the package calls only `nb200::*` ops by name and runs without Python --
+  the reference instead embeds its generated Triton kernels in the package.
 
 Differences from the reference, by design:
-* the ops are `torch.library.custom_op`s around C ABI launches instead of `triton_op`s;
-  `as_triton_op`, `triton_op_name` and `_TRITON_OPS` remain as aliases of the CUDA names so the
-  reference's callers keep working;
+* the ops are composite ops over C++ ops instead of `triton_op`s; `as_triton_op`,
+  `triton_op_name` and `_TRITON_OPS` remain as aliases of the CUDA names so the reference's
+  callers keep working;
 * descriptor validation of segment pooling never traps the GPU: the kernels OR violations into a
-  sticky per-device status word and malformed spans pool to NaN (as the reference kernel itself
-  does). `segment_status()` reads and clears the word; with NEPTUNE_B200_SYNC_CHECKS=1 every call
-  checks it and raises the reference's RuntimeError messages.
+  sticky per-device status word (one word per device, shared by every launch path) and malformed
+  spans pool to NaN (as the reference kernel itself does). `segment_status()` reads and clears the
+  word; with NEPTUNE_B200_SYNC_CHECKS=1 every eager call checks it and raises the reference's
+  RuntimeError messages.
 """
 from __future__ import annotations
 
@@ -32,14 +43,39 @@ from neptune_opt_b200.template import (_on_device, _ptr, _row_last_layout, _vali
 
 _CUDA_OPS: dict[str, object] = {}
 _TRITON_OPS = _CUDA_OPS  # the reference's registry name
+_FRAGMENTS: dict[str, object] = {}
 
 
-def _register(op_name: str, schema: str, impl, fake):
+def _nb200():
+    """torch.ops.nb200 with the C++ region ops registered (libneptune_b200_torch.so)."""
     import torch
 
-    op = torch.library.custom_op(op_name, impl, mutates_args=(), schema=schema)
-    op.register_fake(fake)
-    return op
+    from neptune_opt_b200 import aot
+
+    aot.load()
+    return torch.ops.nb200
+
+
+def _tracing(*tensors) -> bool:
+    """True while fake, meta or functional tensors trace the op (export, AOTInductor, FakeTensorMode)."""
+    from torch._subclasses.fake_tensor import FakeTensor
+    from torch.utils._python_dispatch import is_traceable_wrapper_subclass
+
+    return any(isinstance(t, FakeTensor) or t.device.type == "meta" or is_traceable_wrapper_subclass(t)
+               for t in tensors)
+
+
+def _register(op_name: str, schema: str, body):
+    """Define `lib::name` with `schema`; its one kernel is the CompositeImplicitAutograd `body`."""
+    import torch
+
+    lib, name = op_name.split("::", 1)
+    frag = _FRAGMENTS.get(lib)
+    if frag is None:
+        frag = _FRAGMENTS[lib] = torch.library.Library(lib, "FRAGMENT")
+    frag.define(name + schema)
+    frag.impl(name, body, "CompositeImplicitAutograd")
+    return _overload(lib, op_name)
 
 
 def _overload(lib: str, op_name: str):
@@ -52,7 +88,7 @@ def _overload(lib: str, op_name: str):
 # ---------------------------------------------------------------- scalar skeleton ops
 def as_cuda_op(name: str, block: int | None = None, num_warps: int | None = None, lib: str = "neptune",
                params: dict | None = None, keepdim: bool = False, plan: str = "serial"):
-    """Register (once) and return the custom op for one fold (torch_op.py:16-114)."""
+    """Register (once) and return the op for one fold (torch_op.py:16-114)."""
     validate_plan(plan)
     if name not in SKELETONS:
         raise KeyError(f"unknown skeleton {name!r}; have {sorted(SKELETONS)}")
@@ -68,31 +104,27 @@ def as_cuda_op(name: str, block: int | None = None, num_warps: int | None = None
     if key in _CUDA_OPS:
         return _CUDA_OPS[key]
 
-    import torch
+    from neptune_opt_b200.aot import fold_params
 
-    def _impl(x):
-        _validate_row_last(x)
-        x2, rows, ncols = _row_last_layout(x)
-        shape = x.shape[:-1] + ((1,) if keepdim else ())
-        out = torch.empty(shape, device=x.device, dtype=x.dtype)
-        if isinstance(rows, int) and rows == 0:
-            return out
+    sk_id = SKELETONS[name].id
+    fparams = fold_params(name, values)
+    plan_code = 0 if plan == "serial" else 1
+
+    def _body(x):
+        _validate_row_last(x, metadata=_tracing(x))
         cfg = (block, num_warps)
-        if plan == "serial" and (block is None or num_warps is None):
-            chosen = autotune.best_config(rows, ncols, x.dtype, x.device)
-            cfg = (chosen[0] if block is None else block, chosen[1] if num_warps is None else num_warps)
-        launch_reduction(name, plan, x2, out, rows, ncols, cfg[0], cfg[1], values)
-        return out
-
-    def _fake(x):
-        _validate_row_last(x, metadata=True)
         if plan == "split":
             split_launch_shape(x.shape[-1], block)
-        shape = x.shape[:-1] + ((1,) if keepdim else ())
-        return torch.empty(shape, device=x.device, dtype=x.dtype)
+        elif block is None or num_warps is None:
+            shape = tuple(x.shape)
+            concrete = all(type(d) is int for d in shape)
+            rows = math.prod(shape[:-1]) if concrete else None
+            chosen = (autotune.best_config(rows, shape[-1], x.dtype, x.device) if concrete
+                      else autotune.DEFAULT)
+            cfg = (chosen[0] if block is None else block, chosen[1] if num_warps is None else num_warps)
+        return _nb200().fold(x, sk_id, fparams, keepdim, plan_code, int(cfg[0] or 0), int(cfg[1] or 0))
 
-    op = _register(key, "(Tensor x) -> Tensor", _impl, _fake)
-    op.__name__ = f"{lib}_{key.split('::', 1)[1]}"
+    op = _register(key, "(Tensor x) -> Tensor", _body)
     _CUDA_OPS[key] = op
     return op
 
@@ -103,8 +135,7 @@ as_triton_op = as_cuda_op
 def op_handle(name: str, params: dict | None = None, lib: str = "neptune", keepdim: bool = False,
               block: int | None = None, num_warps: int | None = None, plan: str = "serial"):
     """The OpOverload for a compiled skeleton, for building graph nodes (torch_op.py:117-134)."""
-    op = as_cuda_op(name, block=block, num_warps=num_warps, params=params, lib=lib, keepdim=keepdim, plan=plan)
-    return _overload(lib, f"{lib}::{op.__name__[len(lib) + 1:]}")
+    return as_cuda_op(name, block=block, num_warps=num_warps, params=params, lib=lib, keepdim=keepdim, plan=plan)
 
 
 def cuda_op_name(name: str, lib: str = "neptune") -> str:
@@ -122,21 +153,15 @@ def softmax_op_handle(log: bool = False, lib: str = "neptune"):
     """OpOverload `(Tensor x) -> Tensor` of the fused softmax (log=False) / log_softmax readout."""
     key = (lib, bool(log))
     if key not in _READOUT_OPS:
-        import torch
+        mode = 1 if log else 0
 
-        from neptune_opt_b200.template import run_softmax
+        def _body(x):
+            _validate_row_last(x, metadata=_tracing(x))
+            return _nb200().softmax(x, mode)[0]
 
-        op_name = f"{lib}::{'log_softmax' if log else 'softmax'}_lastdim"
-
-        def _impl(x):
-            return run_softmax(x, log=log)
-
-        def _fake(x):
-            _validate_row_last(x, metadata=True)
-            return torch.empty(x.shape, device=x.device, dtype=x.dtype)
-
-        _READOUT_OPS[key] = _register(op_name, "(Tensor x) -> Tensor", _impl, _fake)
-    return _overload(lib, f"{lib}::{'log_softmax' if log else 'softmax'}_lastdim")
+        _READOUT_OPS[key] = _register(f"{lib}::{'log_softmax' if log else 'softmax'}_lastdim", "(Tensor x) -> Tensor",
+                                      _body)
+    return _READOUT_OPS[key]
 
 
 # ---------------------------------------------------------------- structured RMSNorm
@@ -157,31 +182,20 @@ def as_state_op(name, params=None, plan="serial", lib="neptune"):
     key = (lib, "rms_norm", autotune.parameter_identity(params), plan)
     if key in _STATE_OPS:
         return _STATE_OPS[key]
-    import torch
-
     impl_name = f"state_rms_norm{autotune.parameter_tag(params)}_plan_{plan}"
+    eps_value = float(eps)
 
-    def _impl(x, gamma):
-        shape = validate_rms_inputs(x, gamma, params, plan=plan)
-        out = torch.empty(shape, dtype=x.dtype, device=x.device)
-        if x.numel() == 0:
-            return out
-        launch_rms_norm(x, gamma, out, eps=float(eps), plan=plan)
-        return out
+    def _body(x, gamma):
+        validate_rms_inputs(x, gamma, params, plan=plan, metadata=_tracing(x, gamma))
+        return _nb200().rms_norm(x, gamma, eps_value)
 
-    def _fake(x, gamma):
-        shape = validate_rms_inputs(x, gamma, params, plan=plan, metadata=True)
-        return torch.empty(shape, dtype=x.dtype, device=x.device)
-
-    op = _register(f"{lib}::{impl_name}", "(Tensor x, Tensor gamma) -> Tensor", _impl, _fake)
-    op.__name__ = f"{lib}_{impl_name}"
+    op = _register(f"{lib}::{impl_name}", "(Tensor x, Tensor gamma) -> Tensor", _body)
     _STATE_OPS[key] = op
     return op
 
 
 def state_op_handle(name, params=None, plan="serial", lib="neptune"):
-    op = as_state_op(name, params=params, plan=plan, lib=lib)
-    return _overload(lib, f"{lib}::{op.__name__[len(lib) + 1:]}")
+    return as_state_op(name, params=params, plan=plan, lib=lib)
 
 
 # ---------------------------------------------------------------- ordered segment pooling
@@ -259,19 +273,13 @@ def _sync_checks() -> bool:
     return os.environ.get("NEPTUNE_B200_SYNC_CHECKS", "") not in ("", "0")
 
 
-_STATUS: dict = {}
-
-
 def segment_status_word(device):
-    """The device's sticky descriptor-status word (int32, zero until a violation is recorded)."""
+    """The device's sticky descriptor-status word (int32, zero until a violation is recorded). It is
+    the word the C++ region ops use too, so every launch path records into one word per device."""
     import torch
 
-    key = (device.type, device.index if device.index is not None else torch.cuda.current_device())
-    word = _STATUS.get(key)
-    if word is None:
-        word = torch.zeros(1, dtype=torch.int32, device=device)
-        _STATUS[key] = word
-    return word
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    return _nb200().segment_status_word(index)
 
 
 def segment_status(device=None, clear: bool = True) -> int:
@@ -363,9 +371,7 @@ def run_segment_pool(data, segments, *, reduce="sum", offsets=False, initial=Non
 
 
 def as_segment_op(name, params=None, plan="serial", lib="neptune"):
-    """Two-tensor custom op (torch_op.py:427-457); constants live in the op's identity."""
-    import torch
-
+    """Two-tensor op (torch_op.py:427-457); constants live in the op's identity."""
     params = _segment_params(name, params, plan)
     numeric = {k: v for k, v in params.items() if v is not None}
     identity = (lib, name, params["initial"] is None, autotune.parameter_identity(numeric), plan)
@@ -375,20 +381,22 @@ def as_segment_op(name, params=None, plan="serial", lib="neptune"):
 
     impl_name = f"{name}_serial_h" + hashlib.sha256(repr(identity[1:]).encode()).hexdigest()[-10:]
 
-    def _impl(data, segments):
-        return _launch_segment(name, data, segments, params, plan)
+    reduce_code = 1 if name == "segment_mean" else 0
+    reduce = name.removeprefix("segment_")
 
-    def _fake(data, segments):
-        shape = validate_segment_inputs(data, segments, metadata=True, reduce=name.removeprefix("segment_"),
-                                        plan=plan, **params)
-        return torch.empty(shape, dtype=data.dtype, device=data.device)
+    def _body(data, segments):
+        tracing = _tracing(data, segments)
+        validate_segment_inputs(data, segments, metadata=tracing, reduce=reduce, plan=plan, **params)
+        out = _nb200().segment_pool(data, segments, params["offsets"], reduce_code, params["initial"],
+                                    params["unsafe"])
+        if not tracing and _sync_checks():
+            check_segment_status(segment_status(data.device))
+        return out
 
-    op = _register(f"{lib}::{impl_name}", "(Tensor data, Tensor segments) -> Tensor", _impl, _fake)
-    op.__name__ = f"{lib}_{impl_name}"
+    op = _register(f"{lib}::{impl_name}", "(Tensor data, Tensor segments) -> Tensor", _body)
     _SEGMENT_OPS[identity] = op
     return op
 
 
 def segment_op_handle(name, params=None, plan="serial", lib="neptune"):
-    op = as_segment_op(name, params=params, plan=plan, lib=lib)
-    return _overload(lib, f"{lib}::{op.__name__[len(lib) + 1:]}")
+    return as_segment_op(name, params=params, plan=plan, lib=lib)

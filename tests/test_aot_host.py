@@ -6,13 +6,15 @@ from __future__ import annotations
 import pytest
 
 SCHEMAS = {
-    "fold": "nb200::fold(Tensor x, int skeleton, float[] params, bool keepdim, int plan, int block) -> Tensor",
+    "fold": "nb200::fold(Tensor x, int skeleton, float[] params, bool keepdim, int plan, int block, "
+            "int num_warps=0) -> Tensor",
     "softmax": "nb200::softmax(Tensor x, int mode) -> (Tensor, Tensor)",
     "l2_normalize": "nb200::l2_normalize(Tensor x) -> (Tensor, Tensor)",
     "rms_norm": "nb200::rms_norm(Tensor x, Tensor gamma, float eps) -> Tensor",
     "segment_pool": "nb200::segment_pool(Tensor data, Tensor segments, bool offsets, int reduce, float? initial, "
                     "bool unsafe) -> Tensor",
     "attention": "nb200::attention(Tensor q, Tensor k, Tensor v, bool causal, float scale) -> (Tensor, Tensor)",
+    "segment_status_word": "nb200::segment_status_word(int device) -> Tensor",
 }
 
 

@@ -95,6 +95,40 @@ def test_rms_norm_matches_reference_aten_form(oracle_mod):
         assert_rms_close(got, rms[key + "|out"], dtype)
 
 
+def test_aten_graph_restatements_match_the_reference_outputs():
+    """oracle/aten_graph.py (the reference arm's CPU path): bit-identical to the reference's RMSNorm
+    ATen outputs and segment outputs, and its logsumexp lowering within fp32 rounding of the
+    reference's ATen logsumexp."""
+    import torch
+
+    from oracle import aten_graph
+
+    rms = golden("rms_norm.npz")
+    for key in sorted({k.rsplit("|", 1)[0] for k in rms.files}):
+        dt = getattr(torch, key.split("|")[0])
+        x = torch.from_numpy(rms[key + "|x"]).to(dt)
+        g = torch.from_numpy(rms[key + "|gamma"]).to(dt)
+        got = aten_graph.rms_norm(x, g, 1e-6).float().numpy()
+        assert np.array_equal(got, rms[key + "|out"]), key
+    sm = golden("softmax.npz")
+    x = torch.from_numpy(sm["x"])
+    fin = np.isfinite(sm["logsumexp"])
+    got = aten_graph.logsumexp(x).numpy()
+    assert np.array_equal(np.isnan(got), np.isnan(sm["logsumexp"]))
+    np.testing.assert_allclose(got[fin], sm["logsumexp"][fin], rtol=1e-6)
+    seg = golden("segment.npz")
+    for key in sorted({k.rsplit("|", 1)[0] for k in seg.files}):
+        dtype, view, initial, reduce, kind = key.split("|")
+        if kind != "len" or initial != "None" or view != "poisson":
+            continue
+        data = torch.from_numpy(seg[key + "|data"]).to(getattr(torch, dtype))
+        lengths = torch.from_numpy(seg[key + "|segments"])
+        got = aten_graph.segment_pool(data, lengths, reduce).float().numpy()
+        ref = seg[key + "|out"]
+        assert np.array_equal(np.isnan(got), np.isnan(ref)) and np.array_equal(got[~np.isnan(ref)],
+                                                                              ref[~np.isnan(ref)]), key
+
+
 def test_segment_pool_bit_exact_against_reference(oracle_mod):
     seg = golden("segment.npz")
     keys = sorted({k.rsplit("|", 1)[0] for k in seg.files})
