@@ -99,10 +99,12 @@ const char* nb200_last_error(void);
 const char* nb200_version(void);
 /* Number of nb200 kernel launches issued by this process (for launch accounting). */
 uint64_t nb200_launch_count(void);
-/* Reads and clears the fault bits of the kernels with device-side waits (bit 0: a bounded wait
- * on a bulk copy in a streaming kernel ran out and the kernel stopped early; bit 1: a bounded wait
- * in the attention kernel ran out and its output was left unwritten). Synchronous. No counterpart in the reference, whose
- * Triton kernels have no device-side waits. */
+/* Reads and clears the fault bits of the kernels with device-side waits or checks (bit 0: a
+ * bounded wait on a bulk copy in a streaming kernel ran out and the kernel stopped early; bit 1: a
+ * bounded wait in the attention kernel ran out and its output was left unwritten; bit 2: the peer
+ * merge's bounded wait for the ranks' flags ran out, output unwritten; bit 3: a peer push or merge
+ * found a buffer whose recorded layout differs from the call's, nothing stored or read).
+ * Synchronous. No counterpart in the reference, whose Triton kernels have no device-side waits. */
 int nb200_stream_fault(uint32_t* bits);
 
 /* ------------------------------------------------------------------ a1: serial fold
@@ -178,9 +180,11 @@ int nb200_fold_merge(int skeleton, const nb200_params* params,
 /* The split plan across GPUs without a collective (no counterpart in the reference, which has no
  * multi-GPU path): column shards' chunk states move through NVLink peer memory. Each rank owns an
  * exchange buffer of nb200_peer_buffer_bytes(rows, world, nparts) bytes (device memory, 256-byte
- * aligned, ZEROED once before its first use, then reused across calls) and maps every other rank's
- * buffer with nb200_ipc_handle / nb200_ipc_open (CUDA IPC; the library only maps, it allocates
- * nothing). Per call, in this order on one stream:
+ * aligned, reused across calls), initialises it once with nb200_peer_init (which records the
+ * (rows, world, nparts) layout in the buffer's header and clears its epoch and flags), and maps
+ * every other rank's buffer with nb200_ipc_handle / nb200_ipc_open (CUDA IPC; the library only
+ * maps, it allocates nothing). Every rank initialises before any rank's first push (a barrier
+ * between them). Per call, in this order on one stream:
  *   nb200_fold_partial  -> states[rows][nlocal] of this rank's shard;
  *   nb200_peer_push     -> writes them into slot `rank` (nparts wide, parts past nlocal empty) of
  *                          every rank's buffer and raises this rank's flag there (peers[r] = rank
@@ -190,8 +194,14 @@ int nb200_fold_merge(int skeleton, const nb200_params* params,
  *                          each row's world * nparts states in ascending (rank, part) order into
  *                          out[rows] -- the result of nb200_fold_merge on the gathered states.
  * Every rank makes the same calls in the same order with the same rows and nparts; a call's epoch
- * lives in the buffer, so the sequence may be captured in a CUDA graph and replayed. world <= 8. */
+ * lives in the buffer, so the sequence may be captured in a CUDA graph and replayed. world <= 8.
+ * Layout checks: before storing into a destination, the push kernel compares the call's
+ * (rows, world, nparts) with the layout recorded in this rank's and the destination's header; the
+ * merge compares its own. On a mismatch (or a buffer never initialised) nothing is stored or read,
+ * bit 3 of nb200_stream_fault is set and the output is left unwritten. After fault bit 2 or 3 the
+ * ranks' epochs no longer agree: close the exchange on every rank and set it up again. */
 int64_t nb200_peer_buffer_bytes(int64_t rows, int64_t world, int64_t nparts);
+int nb200_peer_init(void* buffer, int64_t rows, int world, int64_t nparts, void* stream);
 int nb200_peer_push(const nb200_state* states, int64_t rows, int64_t nlocal, int64_t nparts,
                     void* const* peers, int world, int rank, void* buffer, void* stream);
 int nb200_peer_merge(int skeleton, const nb200_params* params, void* buffer, int64_t rows,

@@ -63,6 +63,7 @@ SIGNATURES = {
                                   _i64, _i64, _vp, ctypes.POINTER(NB200Launch), _vp]),
     "nb200_fold_merge": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
     "nb200_peer_buffer_bytes": (_i64, [_i64, _i64, _i64]),
+    "nb200_peer_init": (_int, [_vp, _i64, _int, _i64, _vp]),
     "nb200_peer_push": (_int, [_vp, _i64, _i64, _i64, ctypes.POINTER(ctypes.c_void_p), _int, _int, _vp, _vp]),
     "nb200_peer_merge": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _i64, _i64, _int, _vp, _int, _vp]),
     "nb200_ipc_handle": (_int, [_vp, _vp, ctypes.POINTER(ctypes.c_int64)]),

@@ -286,6 +286,18 @@ int64_t nb200_peer_buffer_bytes(int64_t rows, int64_t world, int64_t nparts) {
     return peer_buffer_bytes(rows, world, nparts);
 }
 
+int nb200_peer_init(void* buffer, int64_t rows, int world, int64_t nparts, void* stream) {
+    if (world < 1 || world > peer_max_world() || rows < 0 || nparts < 1) {
+        set_error("nb200_peer_init: need 1 <= world <= %d, rows >= 0, nparts >= 1", peer_max_world());
+        return NB200_ERR_ARG;
+    }
+    if (!buffer || (reinterpret_cast<uintptr_t>(buffer) & 255u)) {
+        set_error("nb200_peer_init: null or unaligned buffer");
+        return NB200_ERR_ARG;
+    }
+    return launch_peer_init(buffer, rows, nparts, world, (cudaStream_t)stream);
+}
+
 int nb200_peer_push(const nb200_state* states, int64_t rows, int64_t nlocal, int64_t nparts, void* const* peers,
                     int world, int rank, void* buffer, void* stream) {
     if (world < 1 || world > peer_max_world() || rank < 0 || rank >= world) {

@@ -264,20 +264,52 @@ static __device__ unsigned int g_peer_fault = 0u;
 constexpr int kMaxPeers = 8;
 constexpr int64_t kPeerHeaderBytes = 256;
 constexpr long long kPeerWaitCycles = 1ll << 31;
+constexpr unsigned int kPeerMagic = 0x4e425045u;  // "NBPE": written by peer_init_kernel
 struct PeerHeader {
     unsigned int ep;          // epoch of the last completed exchange on this rank
     unsigned int unused;
     unsigned int merge_done;  // the same for the merge
     unsigned int pad;
     unsigned int flag[kMaxPeers];
+    // The layout this buffer was sized and initialised for (nb200_peer_init). Every push checks the
+    // destination's layout and every merge its own before touching the slots: a call whose
+    // (rows, world, nparts) differ, or a buffer never initialised, stores nothing.
+    long long rows;
+    long long nparts;
+    int world;
+    unsigned int magic;
 };
 static_assert(sizeof(PeerHeader) <= kPeerHeaderBytes, "peer header");
 struct PeerPtrs {
     unsigned char* p[kMaxPeers];  // every rank's exchange buffer as mapped in this process
 };
 
-// One CTA per destination rank: CTA r writes this rank's states into rank r's buffer, fences at
-// system scope and raises flag[rank] there, so each flag follows exactly the stores it announces.
+__device__ __forceinline__ bool peer_layout_ok(const unsigned char* buf, int64_t rows, int64_t nparts, int world) {
+    const volatile PeerHeader* h = reinterpret_cast<const volatile PeerHeader*>(buf);
+    return h->magic == kPeerMagic && h->rows == rows && h->nparts == nparts && h->world == world;
+}
+
+// Records the layout in a buffer's header and clears its epoch, counters and flags (one thread).
+__global__ void peer_init_kernel(unsigned char* buf, int64_t rows, int64_t nparts, int world) {
+    pdl_wait();
+    pdl_trigger();
+    PeerHeader* h = reinterpret_cast<PeerHeader*>(buf);
+    h->ep = 0u;
+    h->unused = 0u;
+    h->merge_done = 0u;
+    h->pad = 0u;
+    for (int r = 0; r < kMaxPeers; ++r) h->flag[r] = 0u;
+    h->rows = rows;
+    h->nparts = nparts;
+    h->world = world;
+    __threadfence_system();
+    h->magic = kPeerMagic;
+    __threadfence_system();
+}
+
+// One CTA per destination rank: CTA r checks rank r's recorded layout, writes this rank's states
+// into rank r's buffer, fences at system scope and raises flag[rank] there, so each flag follows
+// exactly the stores it announces. A destination whose layout differs gets nothing (fault bit 3).
 constexpr int kPushThreads = 512;
 __global__ void __launch_bounds__(kPushThreads)
 peer_push_kernel(const nb200_state* __restrict__ states, int64_t rows, int64_t nlocal, int64_t nparts,
@@ -288,6 +320,13 @@ peer_push_kernel(const nb200_state* __restrict__ states, int64_t rows, int64_t n
     const unsigned int e = *reinterpret_cast<const volatile unsigned int*>(&h->ep) + 1u;
     const int64_t par = e & 1u, n = rows * nparts;
     unsigned char* dst = peers.p[blockIdx.x];
+    __shared__ int layout_ok;
+    if (threadIdx.x == 0) {
+        layout_ok = peer_layout_ok(own, rows, nparts, world) && peer_layout_ok(dst, rows, nparts, world);
+        if (!layout_ok) atomicOr(&g_peer_fault, 8u);
+    }
+    __syncthreads();
+    if (!layout_ok) return;
     float4* slots = reinterpret_cast<float4*>(dst + kPeerHeaderBytes);
     for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
         const int64_t row = i / nparts, part = i - row * nparts;
@@ -310,6 +349,10 @@ peer_merge_kernel(unsigned char* own, T* __restrict__ out, int64_t rows, int64_t
     pdl_wait();
     pdl_trigger();
     PeerHeader* h = reinterpret_cast<PeerHeader*>(own);
+    if (!peer_layout_ok(own, rows, nparts, world)) {  // nothing read, nothing written, epoch kept
+        if (threadIdx.x == 0) atomicOr(&g_peer_fault, 8u);
+        return;
+    }
     const unsigned int e = *reinterpret_cast<volatile unsigned int*>(&h->ep) + 1u;
     // Thread r waits for rank r's flag, so the ranks' system-scope polls overlap.
     bool ok = true;
@@ -650,6 +693,12 @@ int64_t peer_buffer_bytes(int64_t rows, int64_t world, int64_t nparts) {
 }
 
 int peer_max_world() { return kMaxPeers; }
+
+int launch_peer_init(void* buffer, int64_t rows, int64_t nparts, int world, cudaStream_t st) {
+    launch_pdl(peer_init_kernel, 1, 1, 0, st, static_cast<unsigned char*>(buffer), rows, nparts, world);
+    count_launch();
+    return finish_launch("nb200_peer_init");
+}
 
 int launch_peer_push(const nb200_state* states, int64_t rows, int64_t nlocal, int64_t nparts, void* const* peers,
                      int world, int rank, void* own, cudaStream_t st) {

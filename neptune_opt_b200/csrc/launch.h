@@ -27,6 +27,7 @@ int launch_merge(int sk, const Params& p, const nb200_state* states, int64_t row
 // Column-sharded split plan across GPUs: chunk states exchanged through peer memory (fold.cu).
 int64_t peer_buffer_bytes(int64_t rows, int64_t world, int64_t nparts);
 int peer_max_world();
+int launch_peer_init(void* buffer, int64_t rows, int64_t nparts, int world, cudaStream_t st);
 int launch_peer_push(const nb200_state* states, int64_t rows, int64_t nlocal, int64_t nparts, void* const* peers,
                      int world, int rank, void* own, cudaStream_t st);
 int launch_peer_merge(int sk, const Params& p, void* own, int64_t rows, int64_t nparts, int world, void* out,

@@ -127,12 +127,21 @@ def _cuda_merge(name, params, states, out):
 class PeerExchange:
     """Exchange buffers of the column-sharded split plan, mapped across the ranks of `group`.
 
-    Every rank allocates one zeroed buffer of `nb200_peer_buffer_bytes(rows, world, nparts)` bytes on
-    its GPU and maps the others' with CUDA IPC (handles swapped once with all_gather_object). A
-    `sharded_split_fold(..., exchange=ex)` call then moves the chunk states with two kernels --
-    stores into every peer's buffer plus a flag, and a merge that waits for all flags -- instead of
-    a collective. `nparts` is the per-rank slot width: the largest number of chunks any rank's shard
-    has. Create it on every rank of the group (it synchronises them) and `close()` it on every rank.
+    Every rank allocates one buffer of `nb200_peer_buffer_bytes(rows, world, nparts)` bytes on its
+    GPU, records the layout in it (`nb200_peer_init`) and maps the others' with CUDA IPC (handles
+    swapped once with all_gather_object). A `sharded_split_fold(..., exchange=ex)` call then moves
+    the chunk states with two kernels -- stores into every peer's buffer plus a flag, and a merge
+    that waits for all flags -- instead of a collective. `nparts` is the per-rank slot width: the
+    largest number of chunks any rank's shard has. Create it on every rank of the group (it
+    synchronises them) and `close()` it on every rank.
+
+    Faults: the merge's wait for the ranks' flags is bounded (about a second); when it runs out
+    (a rank did not push) the kernel sets bit 2 of `nb200_stream_fault` and leaves the output
+    unwritten, and a call whose layout differs from a buffer's sets bit 3 and stores nothing.
+    Nothing on the host notices by itself: pass `check=True` to `sharded_split_fold` (it
+    synchronises and raises), or read `neptune_opt_b200._lib.stream_fault()`. After either fault
+    the ranks' epochs disagree, so this exchange refuses further calls: close it on every rank and
+    build a new one.
     """
 
     def __init__(self, rows: int, nparts: int, group=None, device=None):
@@ -147,6 +156,7 @@ class PeerExchange:
         self.rows, self.nparts = int(rows), int(nparts)
         self._lib = lib = _lib.load()
         self._opened, self.peers = [], None
+        self.faulted = False
         nbytes = int(lib.nb200_peer_buffer_bytes(self.rows, self.world, self.nparts))
         if nbytes < 0:
             raise ValueError(f"no peer exchange for rows={rows}, world={self.world}, nparts={nparts} (world <= 8)")
@@ -158,11 +168,15 @@ class PeerExchange:
             self._storage = torch.zeros(nbytes + 256, dtype=torch.uint8, device=device)
             pad = (-self._storage.data_ptr()) % 256
             self.buffer = self._storage[pad:pad + nbytes]
+            with torch.cuda.device(device):
+                _lib.check(lib.nb200_peer_init(ctypes.c_void_p(self.buffer.data_ptr()), self.rows, self.world,
+                                               self.nparts, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)),
+                           "peer exchange init")
             handle = (ctypes.c_char * 64)()
             offset = ctypes.c_int64()
             _lib.check(lib.nb200_ipc_handle(ctypes.c_void_p(self.buffer.data_ptr()), handle, ctypes.byref(offset)),
                        "peer exchange handle")
-            torch.cuda.synchronize(device)  # the buffer is zero before any peer can write into it
+            torch.cuda.synchronize(device)  # the layout is recorded before any peer can write into it
             mine = (bytes(handle), int(offset.value), self.rows, self.nparts)
         except Exception as exc:  # noqa: BLE001 -- reported on every rank below
             mine = ("error", f"rank {self.rank}: {exc}")
@@ -204,12 +218,23 @@ class PeerExchange:
         from neptune_opt_b200.skeletons import SKELETONS, checked_params
         from neptune_opt_b200.template import _on_device, current_stream, dtype_code
 
+        import torch
+
         if self.peers is None:
             raise RuntimeError("the peer exchange is closed")
+        if self.faulted:
+            raise RuntimeError("the peer exchange faulted (a bounded wait ran out or a layout differed); "
+                               "close it on every rank and set up a new one")
+        if states.dtype != torch.int32 or states.dim() != 3 or states.shape[2] != 4 or not states.is_contiguous():
+            raise ValueError("states must be a contiguous int32 [rows, nlocal, 4] tensor of chunk states")
         rows, nlocal = states.shape[0], states.shape[1]
         if rows != self.rows or nlocal > self.nparts:
             raise ValueError(f"states [{rows}, {nlocal}] do not fit the exchange ({self.rows} rows, "
                              f"{self.nparts} parts per rank)")
+        if out.dim() != 1 or out.numel() != rows or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous [{rows}] tensor")
+        if states.device != self.buffer.device or out.device != self.buffer.device:
+            raise ValueError(f"states and out must be on the exchange's device {self.buffer.device}")
         p = _lib.params_struct(checked_params(name, params))
         lib = self._lib
         with _on_device(states.device):
@@ -239,7 +264,7 @@ class PeerExchange:
 
 
 def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: int = 16384, group=None,
-                       partial_fn=None, merge_fn=None, widths=None, exchange=None):
+                       partial_fn=None, merge_fn=None, widths=None, exchange=None, check: bool = False):
     """Fold rows whose columns are sharded across the ranks of `group`, rank order = column order.
 
     Each rank passes its own [rows, width_r] block (the ranks' blocks concatenated along columns in
@@ -253,7 +278,9 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
     rank order) skips the width exchange -- and its host synchronisation -- when the caller knows
     the layout, as a steady-state loop does. With `exchange` (a PeerExchange whose slot width is the
     largest rank's chunk count) the states move through NVLink peer memory instead of an
-    all-gather; the result is the same bit for bit.
+    all-gather; the result is the same bit for bit. The exchange's output starts as NaN, so a merge
+    whose bounded wait ran out leaves NaN rather than stale memory; `check=True` synchronises after
+    the merge and raises if a wait ran out or a layout differed (marking the exchange unusable).
     """
     import torch
     import torch.distributed as td
@@ -285,8 +312,19 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
         if exchange.nparts != max_parts or exchange.world != world:
             raise ValueError(f"the exchange holds {exchange.nparts} parts per rank for {exchange.world} ranks; "
                              f"this layout needs {max_parts} for {world}")
-        out = torch.empty(rows, dtype=x_shard.dtype, device=x_shard.device)
-        return exchange.exchange_and_merge(name, params, local, out)
+        out = torch.full((rows,), float("nan"), dtype=x_shard.dtype, device=x_shard.device)
+        exchange.exchange_and_merge(name, params, local, out)
+        if check:
+            from neptune_opt_b200 import _lib
+
+            bits = _lib.stream_fault()
+            if bits & 0xC:
+                exchange.faulted = True
+                raise RuntimeError(f"peer exchange fault (bits {bits:#x}): "
+                                   + ("a rank's flag never arrived; " if bits & 4 else "")
+                                   + ("a buffer's layout differs from the call's; " if bits & 8 else "")
+                                   + "close the exchange on every rank and set up a new one")
+        return out
     if local.shape[1] < max_parts:  # pad with empty (seen = 0) states
         pad = torch.zeros(rows, max_parts - local.shape[1], 4, dtype=local.dtype, device=local.device)
         pad[..., 0] = torch.tensor(float("-inf")).view(torch.int32) if local.dtype == torch.int32 else 0

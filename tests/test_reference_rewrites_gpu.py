@@ -107,6 +107,7 @@ for name in {[j[0] for j in jobs]!r}:
     args = [t.cuda() for t in torch.load({str(tmp_path)!r} + "/" + name + ".args.pt")]
     runner = torch._inductor.aoti_load_package({str(tmp_path)!r} + "/" + name + ".pt2")
     out = runner(*args)
+    out = list(out) if isinstance(out, (list, tuple)) else [out]
     torch.cuda.synchronize()
     torch.save([t.cpu() for t in out], {str(tmp_path)!r} + "/" + name + ".out.pt")
 assert not any(m.startswith("neptune_opt_b200") for m in sys.modules)
