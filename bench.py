@@ -57,7 +57,8 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--region", default=None,
                     help="time one region only (rms_norm, softmax_lse, logsumexp, l2_normalize, "
-                         "wide_logsumexp_split, segment_sum, segment_mean, attention, attention_causal) "
+                         "wide_logsumexp_split, segment_sum, segment_mean, attention, attention_causal, "
+                         "lse_1x262144, rms_1x65536, lse_256x16384) "
                          "and print its line; "
                          "used for ncu captures of a single kernel")
     ap.add_argument("--attention-batch", type=int, default=8,
@@ -335,7 +336,46 @@ def make_attention(torch, NB, seed, causal=False, batch=8):
                     f"{'causal' if causal else 'non-causal'} -> o bf16, lse fp32 (inputs {3 * b * h * s * d * 2 >> 20} MiB > L2)"}
 
 
-def make_sharded_split(torch, NB, seed, dist, peer=False):
+def make_small(torch, NB, seed, kind):
+    """The reference's published small shapes (README: logsumexp fp32 (1, 262144), RMSNorm fp32
+    (1, 65536), logsumexp fp32 256 x 16384) through the library's default launch, and for the two
+    single rows the launches they replace: the split plan's two launches (16K-column chunks, then
+    the merge) and one CTA of 512 threads per row. Inputs rotate over more than 126 MB."""
+    import ctypes
+
+    lib = NB._lib.load()
+    rows, ncols = {"lse_1x262144": (1, 262144), "rms_1x65536": (1, 65536), "lse_256x16384": (256, 16384)}[kind]
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    per = rows * ncols * 4
+    nbuf = max(2, -(-L2_BYTES // per) + 1)
+    xs = [torch.randn(rows, ncols, device="cuda", generator=g) * 2.0 for _ in range(nbuf)]
+    out = torch.empty(rows, ncols, device="cuda") if kind.startswith("rms") else torch.empty(rows, device="cuda")
+    gamma = 1 + 0.1 * torch.randn(ncols, device="cuda", generator=g)
+    stream = lambda: ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)  # noqa: E731
+    cta = NB._lib.launch_struct(NB._lib.VARIANT_CTA_ROW, 512, 0, 0)
+
+    def step_for(how):
+        def step(i):
+            x = xs[i % nbuf]
+            if kind.startswith("rms"):
+                NB.template.launch_rms_norm(x, gamma, out, eps=1e-6, launch=cta if how == "cta_row" else None)
+            elif how == "split":
+                NB.template.launch_reduction("logsumexp", "split", x, out, rows, ncols, 16384, 8, {"tiny": 0.0})
+            elif how == "cta_row":
+                p = NB._lib.params_struct({"tiny": 0.0})
+                NB._lib.check(lib.nb200_fold(0, ctypes.byref(p), ctypes.c_void_p(x.data_ptr()), 0, rows, ncols, ncols,
+                                             1, ctypes.c_void_p(out.data_ptr()), ctypes.byref(cta), stream()), "fold")
+            else:
+                NB.template.launch_reduction("logsumexp", "serial", x, out, rows, ncols, None, None, {"tiny": 0.0})
+        return step
+
+    nbytes = rows * ncols * 4 * (2 if kind.startswith("rms") else 1) + (ncols * 4 if kind.startswith("rms") else rows * 4)
+    return {"name": kind, "step": step_for("default"), "bytes": nbytes, "rows": rows, "launches": 1, "buffers": nbuf,
+            "alternatives": {} if rows > 1 else {"split_ms": step_for("split"), "cta_row_ms": step_for("cta_row")},
+            "desc": f"{'rms_norm' if kind.startswith('rms') else 'logsumexp'} fp32 [{rows},{ncols}] (reference README shape)"}
+
+
+def make_sharded_split(torch, NB, seed, dist, peer=False, fused=True):
     """BASELINE config 3b across GPUs: the columns of bf16 [512, 262144] split into one shard per
     rank; each rank folds its shard into 16K-column chunk states, which move to every rank -- one
     NCCL all-gather, or (peer=True) stores into every rank's exchange buffer over NVLink with a flag
@@ -359,12 +399,15 @@ def make_sharded_split(torch, NB, seed, dist, peer=False):
 
     def step(i):
         sharded_split_fold("logsumexp", xs[i % 2], ncols, params={"tiny": 0.0}, chunk=block, widths=[width] * n,
-                           exchange=ex)
+                           exchange=ex, fused=fused)
 
-    how = ("states stored into every rank's exchange buffer over NVLink, one flag per rank, merge waits "
-           "for all flags" if peer else "states all-gathered over NCCL")
-    return {"name": "wide_logsumexp_split_sharded" + ("_peer" if peer else ""), "step": step,
-            "bytes": rows * ncols * 2 + rows * 2, "rows": rows, "launches": 3 if peer else 2, "buffers": 2,
+    how = (("one cooperative launch: fold, stores into every rank's exchange buffer over NVLink, flags, wait, "
+            "merge" if fused else "partial fold, push kernel (stores + flag per rank), merge kernel (waits for "
+            "all flags)") if peer else "states all-gathered over NCCL")
+    name = "wide_logsumexp_split_sharded" + (("_peer" if fused else "_peer_3launch") if peer else "")
+    return {"name": name, "step": step,
+            "bytes": rows * ncols * 2 + rows * 2, "rows": rows, "launches": (1 if fused else 3) if peer else 2,
+            "buffers": 2,
             "exchange": ex,
             "desc": f"logsumexp bf16 x[{rows},{ncols}] N(0,3^2), columns sharded over {n} GPUs ({width} each), "
                     f"{block}-column chunk states {how}, merged in rank order"}
@@ -693,6 +736,9 @@ REGION_MAKERS = {
     "segment_mean": lambda t, nb, s: make_segments(t, nb, s, "mean"),
     "attention": make_attention,
     "attention_causal": lambda t, nb, s, **kw: make_attention(t, nb, s, causal=True, **kw),
+    "lse_1x262144": lambda t, nb, s: make_small(t, nb, s, "lse_1x262144"),
+    "rms_1x65536": lambda t, nb, s: make_small(t, nb, s, "rms_1x65536"),
+    "lse_256x16384": lambda t, nb, s: make_small(t, nb, s, "lse_256x16384"),
 }
 REGION_OPTIONS = {"attention": ("attention_batch", "batch"), "attention_causal": ("attention_batch", "batch")}
 
@@ -804,6 +850,19 @@ def main():
                                  "rows_per_s": round(n * r["rows"] / (rms_ * 1e-3), 1)}
             del r
             torch.cuda.empty_cache()
+        for kind in ("lse_1x262144", "rms_1x65536", "lse_256x16384"):
+            r = make_small(torch, NB, 2300 + dist.rank, kind)
+            sms_, _ = time_steps(torch, dist, r["step"], max(args.steps, 50), max(3, args.warmup))
+            rec = hbm_region(r, sms_, n, peaks)
+            for key, alt in r["alternatives"].items():
+                if kind.startswith("rms") and key == "split_ms":
+                    continue  # RMSNorm's split plan is the same one-launch kernel
+                ams_, _ = time_steps(torch, dist, alt, max(args.steps, 50), max(3, args.warmup))
+                rec[key] = round(ams_, 5)
+            regions[r["name"]] = rec
+            detail[r["name"]] = {"workload": r["desc"], "l2_rotation_buffers": r["buffers"]}
+            del r
+            torch.cuda.empty_cache()
         for causal in (False, True):
             # Burst: 10 launches (~20 ms), the regime of the burst GEMM peak. Sustained: 100
             # launches back to back (~0.2 s under the power cap), against the sustained peak.
@@ -829,8 +888,8 @@ def main():
                 detail[r["name"]] = {"workload": r["desc"]}
                 del r
                 torch.cuda.empty_cache()
-            for peer in (False, True):
-                r = make_sharded_split(torch, NB, 2600, dist, peer=peer)
+            for peer, fused in ((False, True), (True, True), (True, False)):
+                r = make_sharded_split(torch, NB, 2600, dist, peer=peer, fused=fused)
                 if r is None:
                     continue
                 steps = min(args.steps, 50)

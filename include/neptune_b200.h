@@ -74,7 +74,10 @@ typedef enum {
     NB200_VARIANT_AUTO = 0,
     NB200_VARIANT_WARP_ROW = 1, /* one warp folds one row, register-resident chunks     */
     NB200_VARIANT_CTA_ROW = 2,  /* one CTA folds one row                                 */
-    NB200_VARIANT_STREAM = 3    /* bulk-copy staged rows (contiguous, 16-byte aligned)   */
+    NB200_VARIANT_STREAM = 3,   /* bulk-copy staged rows (contiguous, 16-byte aligned)   */
+    NB200_VARIANT_CLUSTER = 4   /* one thread-block cluster per row, CTA states merged   */
+                                /* through distributed shared memory (contiguous,        */
+                                /* 16-byte aligned rows; folds and RMSNorm)              */
 } nb200_variant;
 
 typedef struct {
@@ -82,7 +85,8 @@ typedef struct {
     int32_t threads;        /* CTA size (64..512, x32); for NB200_VARIANT_STREAM the   */
                             /* number of warps, each owning its own ring of stages    */
     int32_t ctas_per_sm;    /* persistent grid = SMs * ctas_per_sm (0: default)       */
-    int32_t stages;         /* NB200_VARIANT_STREAM: stages per warp ring (0: fit)    */
+    int32_t stages;         /* NB200_VARIANT_STREAM: stages per warp ring (0: fit);   */
+                            /* NB200_VARIANT_CLUSTER: CTAs per row, 2..16 (0: chosen) */
 } nb200_launch;
 
 /* One partial state of the repaired fold (emitters.py:436-519): raw producer value,
@@ -206,6 +210,18 @@ int nb200_peer_push(const nb200_state* states, int64_t rows, int64_t nlocal, int
                     void* const* peers, int world, int rank, void* buffer, void* stream);
 int nb200_peer_merge(int skeleton, const nb200_params* params, void* buffer, int64_t rows,
                      int64_t nparts, int world, void* out, int dtype, void* stream);
+/* The same call in ONE launch (no counterpart in the reference): the partial fold of this rank's
+ * column shard x[rows, ncols_shard] (contiguous rows, 16-byte aligned, row stride, width and
+ * chunk_cols multiples of 16 bytes), the stores of its chunk states into every rank's buffer, the
+ * flags and the merge of nb200_fold_partial + nb200_peer_push + nb200_peer_merge, in one
+ * cooperative grid (every CTA resident, so the grid's in-kernel wait for the flags cannot keep its
+ * own last CTA from running). ncols_total (all ranks' columns) sets the skeletons' 1/N as in
+ * nb200_fold_partial. Same buffers, layout checks, fault bits, epochs, parities and protocol as
+ * the push/merge pair (the two forms may be mixed, across ranks and across calls), and the same
+ * result bit for bit. */
+int nb200_peer_fold(int skeleton, const nb200_params* params, const void* x, int dtype, int64_t rows,
+                    int64_t ncols_total, int64_t ncols_shard, int64_t stride_row, int64_t chunk_cols, int64_t nparts,
+                    void* const* peers, int world, int rank, void* buffer, void* out, void* stream);
 /* CUDA IPC of a device allocation: handle (64 bytes) and the byte offset of ptr inside it; open
  * maps a peer's allocation (base; add the peer's offset), close unmaps it. */
 int nb200_ipc_handle(const void* ptr, void* handle, int64_t* offset);

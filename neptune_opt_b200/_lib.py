@@ -23,7 +23,7 @@ NB200_ERR_UNSUPPORTED = -5
 DTYPE_CODES = {"float32": 0, "bfloat16": 1, "float16": 2}
 INDEX_CODES = {"int32": 0, "int64": 1}
 
-VARIANT_AUTO, VARIANT_WARP_ROW, VARIANT_CTA_ROW, VARIANT_STREAM = 0, 1, 2, 3
+VARIANT_AUTO, VARIANT_WARP_ROW, VARIANT_CTA_ROW, VARIANT_STREAM, VARIANT_CLUSTER = 0, 1, 2, 3, 4
 
 
 class NB200Params(ctypes.Structure):
@@ -64,6 +64,8 @@ SIGNATURES = {
     "nb200_fold_merge": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _i64, _i64, _i64, _i64, _vp, _int, _vp]),
     "nb200_peer_buffer_bytes": (_i64, [_i64, _i64, _i64]),
     "nb200_peer_init": (_int, [_vp, _i64, _int, _i64, _vp]),
+    "nb200_peer_fold": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _int, _i64, _i64, _i64, _i64, _i64, _i64,
+                               ctypes.POINTER(ctypes.c_void_p), _int, _int, _vp, _vp, _vp]),
     "nb200_peer_push": (_int, [_vp, _i64, _i64, _i64, ctypes.POINTER(ctypes.c_void_p), _int, _int, _vp, _vp]),
     "nb200_peer_merge": (_int, [_int, ctypes.POINTER(NB200Params), _vp, _i64, _i64, _int, _vp, _int, _vp]),
     "nb200_ipc_handle": (_int, [_vp, _vp, ctypes.POINTER(ctypes.c_int64)]),

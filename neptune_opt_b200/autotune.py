@@ -12,8 +12,10 @@ candidate must clear -- but the pair now selects a CUDA launch:
   kernels below;
 * ``num_warps == 1``: one warp folds one row (persistent CTAs of 8 warps, row chunks resident in
   registers, no shared memory or barriers);
-* ``num_warps >= 2``: one CTA of ``32 * num_warps`` threads folds one row (cross-warp reduction
-  through shared memory);
+* ``2 <= num_warps <= 16``: one CTA of ``32 * num_warps`` threads folds one row (cross-warp
+  reduction through shared memory);
+* ``num_warps == 32``: one thread-block cluster folds one row (up to 16 CTAs of 8 warps, their
+  states merged through distributed shared memory in one launch; contiguous aligned rows);
 * ``block`` is the split plan's chunk width in columns (one CTA per chunk). The serial kernels size
   their register tile from the row width themselves, so for the serial plan ``block`` only takes
   part in the operator's identity.
@@ -26,7 +28,7 @@ import dataclasses
 import hashlib
 import math
 
-from neptune_opt_b200._lib import VARIANT_CTA_ROW, VARIANT_WARP_ROW, launch_struct
+from neptune_opt_b200._lib import VARIANT_CLUSTER, VARIANT_CTA_ROW, VARIANT_WARP_ROW, launch_struct
 
 # Every configuration the search may choose from.
 CANDIDATES: tuple = (
@@ -35,6 +37,7 @@ CANDIDATES: tuple = (
     (4096, 4), (16384, 4),
     (4096, 8), (16384, 8),
     (16384, 16),
+    (16384, 32),
 )
 
 # The split plan's chunk width when nothing else is known: 16K columns per CTA (32 KB of bf16).
@@ -168,6 +171,8 @@ def launch_for(cfg) -> object | None:
         return None
     if warps <= 1:
         return launch_struct(VARIANT_WARP_ROW, 0, 0)
+    if warps >= 32:
+        return launch_struct(VARIANT_CLUSTER, 0, 0, 0)
     return launch_struct(VARIANT_CTA_ROW, 32 * int(warps), 0)
 
 

@@ -106,12 +106,17 @@ int check_rows(const void* x, int dtype, int64_t rows, int64_t ncols, const void
 
 int check_launch(const nb200_launch* L) {
     if (!L) return NB200_OK;
-    if (L->variant < 0 || L->variant > NB200_VARIANT_STREAM) { set_error("unknown launch variant %d", L->variant); return NB200_ERR_ARG; }
+    if (L->variant < 0 || L->variant > NB200_VARIANT_CLUSTER) { set_error("unknown launch variant %d", L->variant); return NB200_ERR_ARG; }
     if (L->threads && (L->threads < 64 || L->threads > 512 || L->threads % 32)) {
         set_error("launch threads must be a multiple of 32 in [64, 512]"); return NB200_ERR_ARG;
     }
     if (L->ctas_per_sm < 0 || L->ctas_per_sm > 32) { set_error("ctas_per_sm must be in [0, 32]"); return NB200_ERR_ARG; }
-    if (L->stages < 0 || L->stages > 8) { set_error("stages must be in [0, 8]"); return NB200_ERR_ARG; }
+    if (L->variant == NB200_VARIANT_CLUSTER) {
+        if (L->stages != 0 && (L->stages < 2 || L->stages > 16)) {
+            set_error("cluster launches take 2..16 CTAs per row (stages field), or 0 to choose");
+            return NB200_ERR_ARG;
+        }
+    } else if (L->stages < 0 || L->stages > 8) { set_error("stages must be in [0, 8]"); return NB200_ERR_ARG; }
     return NB200_OK;
 }
 
@@ -322,6 +327,39 @@ int nb200_peer_push(const nb200_state* states, int64_t rows, int64_t nlocal, int
         return NB200_ERR_ARG;
     }
     return launch_peer_push(states, rows, nlocal, nparts, peers, world, rank, buffer, (cudaStream_t)stream);
+}
+
+int nb200_peer_fold(int skeleton, const nb200_params* params, const void* x, int dtype, int64_t rows,
+                    int64_t ncols_total, int64_t ncols_shard, int64_t stride_row, int64_t chunk_cols, int64_t nparts,
+                    void* const* peers, int world, int rank, void* buffer, void* out, void* stream) {
+    nb200_params q;
+    int rc = check_params(skeleton, params, &q);
+    if (rc) return rc;
+    if (!valid_dtype(dtype)) { set_error("nb200_peer_fold: unsupported dtype %d", dtype); return NB200_ERR_ARG; }
+    if (world < 1 || world > peer_max_world() || rank < 0 || rank >= world) {
+        set_error("nb200_peer_fold: need 1 <= world <= %d and 0 <= rank < world", peer_max_world());
+        return NB200_ERR_ARG;
+    }
+    if (rows < 0 || ncols_shard < 1 || ncols_total < ncols_shard || chunk_cols < 1 || nparts < 1 || stride_row < 0) {
+        set_error("nb200_peer_fold: need rows >= 0, 1 <= ncols_shard <= ncols_total, chunk_cols >= 1, nparts >= 1");
+        return NB200_ERR_ARG;
+    }
+    if (!peers || !buffer || (rows > 0 && (!x || !out))) {
+        set_error("nb200_peer_fold: null pointer");
+        return NB200_ERR_ARG;
+    }
+    for (int r = 0; r < world; ++r)
+        if (!peers[r] || (reinterpret_cast<uintptr_t>(peers[r]) & 255u)) {
+            set_error("nb200_peer_fold: exchange buffer of rank %d is null or not 256-byte aligned", r);
+            return NB200_ERR_ARG;
+        }
+    if (peers[rank] != buffer) {
+        set_error("nb200_peer_fold: peers[rank] must be this rank's own buffer");
+        return NB200_ERR_ARG;
+    }
+    if (rows == 0) return NB200_OK;
+    return launch_peer_fold(skeleton, make_params(q, ncols_total), x, dtype, rows, ncols_shard, stride_row, chunk_cols,
+                            nparts, peers, world, rank, buffer, out, (cudaStream_t)stream);
 }
 
 int nb200_peer_merge(int skeleton, const nb200_params* params, void* buffer, int64_t rows, int64_t nparts,

@@ -7,6 +7,7 @@
 // template.py:137-165 (launch template.py:368-390).
 #include "fold.cuh"
 #include "launch.h"
+#include "span.cuh"
 
 namespace nb200 {
 
@@ -267,7 +268,7 @@ constexpr long long kPeerWaitCycles = 1ll << 31;
 constexpr unsigned int kPeerMagic = 0x4e425045u;  // "NBPE": written by peer_init_kernel
 struct PeerHeader {
     unsigned int ep;          // epoch of the last completed exchange on this rank
-    unsigned int unused;
+    unsigned int arrive;      // CTAs of the one-launch exchange that have stored their states
     unsigned int merge_done;  // the same for the merge
     unsigned int pad;
     unsigned int flag[kMaxPeers];
@@ -295,7 +296,7 @@ __global__ void peer_init_kernel(unsigned char* buf, int64_t rows, int64_t npart
     pdl_trigger();
     PeerHeader* h = reinterpret_cast<PeerHeader*>(buf);
     h->ep = 0u;
-    h->unused = 0u;
+    h->arrive = 0u;
     h->merge_done = 0u;
     h->pad = 0u;
     for (int r = 0; r < kMaxPeers; ++r) h->flag[r] = 0u;
@@ -378,6 +379,89 @@ peer_merge_kernel(unsigned char* own, T* __restrict__ out, int64_t rows, int64_t
         const int64_t gid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
         const int64_t ng = (int64_t)gridDim.x * (blockDim.x >> 5);
         for (int64_t r = gid; r < rows; r += ng) {
+            const St s = merge_row<S, true>(slots + r * total, total, 1, lane, p);
+            if (lane == 0) out[r] = Elem<T>::from_f(finalize<S>(s, p));
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(&h->merge_done, 1u) == gridDim.x - 1) {
+        atomicExch(&h->merge_done, 0u);
+        atomicExch(&h->ep, e);
+    }
+}
+
+// One launch per call of the column-sharded split (nb200_peer_fold): the partial fold, the
+// exchange and the merge of the push / merge pair above in a single cooperative grid.
+//   1. Each warp folds span items of this rank's shard (the split plan's span fold, so the states
+//      are bit-identical to nb200_fold_partial's) and lanes 0..world-1 store the item's state into
+//      slot `rank` of every rank's buffer (parts past this rank's chunk count are stored empty).
+//   2. Each CTA fences at system scope and counts itself in; the last CTA raises flag[rank] = e in
+//      every rank's buffer after another system-scope fence.
+//   3. Every CTA waits (bounded) until its own buffer holds every rank's flag for e, then the
+//      grid's warps merge the rows in ascending (rank, part) order; the last CTA records e.
+// The grid is launched cooperatively (all CTAs resident), so CTAs that wait in step 3 cannot keep
+// the last CTA of step 1 from running. Layouts are checked before any store (fault bit 3: nothing
+// stored, no flag raised); a wait that runs out sets fault bit 2 and leaves out unwritten.
+template <int S, typename T>
+__global__ void __launch_bounds__(kLdgThreads)
+peer_fold_kernel(const T* __restrict__ x, LdgSpan pl, int64_t slot_parts, Params p, PeerPtrs peers, int world,
+                 int rank, unsigned char* own, T* __restrict__ out) {
+    PeerHeader* h = reinterpret_cast<PeerHeader*>(own);
+    const int64_t rows = pl.rows;
+    __shared__ int layout_ok;
+    if (threadIdx.x == 0) layout_ok = 1;
+    __syncthreads();
+    if (threadIdx.x < world && !peer_layout_ok(peers.p[threadIdx.x], rows, slot_parts, world)) layout_ok = 0;
+    __syncthreads();
+    if (!layout_ok) {
+        if (threadIdx.x == 0) atomicOr(&g_peer_fault, 8u);
+        return;
+    }
+    const unsigned int e = *reinterpret_cast<volatile unsigned int*>(&h->ep) + 1u;
+    const int64_t par = e & 1u;
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = (int64_t)blockIdx.x * (kLdgThreads / 32) + (threadIdx.x >> 5);
+    const int64_t GW = (int64_t)gridDim.x * (kLdgThreads / 32);
+    const int64_t nitems = rows * slot_parts;
+    for (int64_t item = gw; item < nitems; item += GW) {
+        const int64_t row = item / slot_parts, part = item - row * slot_parts;
+        float4 v = make_float4(-NB200_INF, 0.f, 0.f, 0.f);  // an empty state (parts past this shard)
+        if (part < pl.nparts) {
+            const St w = span_item_state<S, T>(x, pl, row * pl.nparts + part, lane, p);
+            v = make_float4(w.m, w.acc, __int_as_float(w.seen), __int_as_float(w.status));
+        }
+        if (lane < world)
+            reinterpret_cast<float4*>(peers.p[lane] + kPeerHeaderBytes)[((par * rows + row) * world + rank) * slot_parts +
+                                                                        part] = v;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(&h->arrive, 1u) == gridDim.x - 1) {
+        atomicExch(&h->arrive, 0u);
+        __threadfence_system();
+        for (int r = 0; r < world; ++r) {
+            unsigned int* f = &reinterpret_cast<PeerHeader*>(peers.p[r])->flag[rank];
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
+        }
+    }
+    bool ok = true;
+    if (threadIdx.x < world) {
+        const long long t0 = clock64();
+        for (unsigned int it = 0;; ++it) {
+            unsigned int f;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(&h->flag[threadIdx.x]) : "memory");
+            if ((int)(f - e) >= 0) break;
+            if ((it & 63u) == 63u && clock64() - t0 > kPeerWaitCycles) {
+                ok = false;
+                atomicOr(&g_peer_fault, 4u);
+                break;
+            }
+        }
+    }
+    if (__syncthreads_and(ok)) {
+        const int64_t total = (int64_t)world * slot_parts;
+        const nb200_state* slots = reinterpret_cast<const nb200_state*>(own + kPeerHeaderBytes) + par * rows * total;
+        for (int64_t r = gw; r < rows; r += GW) {
             const St s = merge_row<S, true>(slots + r * total, total, 1, lane, p);
             if (lane == 0) out[r] = Elem<T>::from_f(finalize<S>(s, p));
         }
@@ -590,6 +674,41 @@ int peer_merge_dispatch(int sk, unsigned char* own, T* out, int64_t rows, int64_
 }
 
 template <typename T>
+int peer_fold_dispatch(int sk, const T* x, const LdgSpan& pl, int64_t slot_parts, const PeerPtrs& pp, int world,
+                       int rank, unsigned char* own, T* out, const Params& p, cudaStream_t st) {
+    auto go = [&](auto k) {
+        int occ = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kLdgThreads, 0) != cudaSuccess || occ < 1) occ = 1;
+        const int64_t warps = std::max(pl.rows * slot_parts, pl.rows);
+        const int g = (int)std::max<int64_t>(1, std::min<int64_t>((warps + 3) / 4, (int64_t)sm_count() * occ));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)g);
+        cfg.blockDim = dim3(kLdgThreads);
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeCooperative;
+        at[0].val.cooperative = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, k, x, pl, slot_parts, p, pp, world, rank, own, out);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            set_error("nb200_peer_fold: cooperative launch failed: %s", cudaGetErrorString(e));
+            return (int)NB200_ERR_LAUNCH;
+        }
+        count_launch();
+        return finish_launch("nb200_peer_fold");
+    };
+    switch (sk) {
+#define X(S) case S: return go(peer_fold_kernel<S, T>);
+        NB200_SPLIT_SKELETONS(X)
+#undef X
+    }
+    set_error("skeleton %d has no split plan (two-pass skeletons need extended carried state)", sk);
+    return NB200_ERR_UNSUPPORTED;
+}
+
+template <typename T>
 int merge_dispatch(int sk, const nb200_state* states, T* out, int64_t rows, int64_t nparts,
                    int64_t rs, int64_t ps, const Params& p, cudaStream_t st) {
     switch (sk) {
@@ -630,8 +749,40 @@ static bool fold_auto_override(int dtype, int64_t rows, int64_t ncols, nb200_lau
     return false;
 }
 
+// Rows a thread-block cluster per row folds in one launch: contiguous, 16-byte aligned, one-pass
+// skeletons.
+static bool cluster_rows_ok(int sk, const void* x, int dtype, int64_t ncols, int64_t srow, int64_t scol) {
+    const int64_t es = dtype_size(dtype);
+    return sk != NB200_VARIANCE && sk != NB200_STD && scol == 1 && aligned16(x) && (ncols * es) % 16 == 0 &&
+           (srow * es) % 16 == 0;
+}
+
+// Few rows wider than 32 KB: one cluster of CTAs per row (measured faster than one CTA per row or
+// the two-launch split on B200 for such shapes).
+static bool cluster_auto(int sk, const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow, int64_t scol) {
+    return rows >= 1 && rows <= (int64_t)sm_count() / 2 && ncols * (int64_t)dtype_size(dtype) > 32768 &&
+           cluster_rows_ok(sk, x, dtype, ncols, srow, scol);
+}
+
+static int cluster_fold(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t ncols, int64_t srow,
+                        void* out, int csize, cudaStream_t st) {
+    NB200_DTYPE_CASES(dtype, launch_cluster_fold<T>(sk, p, (const T*)x, rows, ncols, srow, (T*)out, csize, st))
+}
+
 int launch_fold(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t ncols,
                 int64_t srow, int64_t scol, void* out, const nb200_launch* L, cudaStream_t st) {
+    const bool want_cluster = L ? L->variant == NB200_VARIANT_CLUSTER
+                                : cluster_auto(sk, x, dtype, rows, ncols, srow, scol);
+    if (want_cluster || (L && L->variant == NB200_VARIANT_AUTO && cluster_auto(sk, x, dtype, rows, ncols, srow, scol))) {
+        const int rc = cluster_rows_ok(sk, x, dtype, ncols, srow, scol)
+                           ? cluster_fold(sk, p, x, dtype, rows, ncols, srow, out, L ? L->stages : 0, st)
+                           : 0;
+        if (rc != 0) return rc < 0 ? rc : NB200_OK;
+        if (L && L->variant == NB200_VARIANT_CLUSTER) {
+            set_error("nb200_fold: the cluster variant needs contiguous 16-byte-aligned rows and a one-pass skeleton");
+            return NB200_ERR_ARG;
+        }
+    }
     nb200_launch chosen;
     if ((!L || L->variant == NB200_VARIANT_AUTO) && fold_auto_override(dtype, rows, ncols, chosen)) L = &chosen;
     if (!L || L->variant == NB200_VARIANT_AUTO || L->variant == NB200_VARIANT_STREAM) {
@@ -714,6 +865,28 @@ int launch_peer_merge(int sk, const Params& p, void* own, int64_t rows, int64_t 
                       int dtype, cudaStream_t st) {
     NB200_DTYPE_CASES(dtype, peer_merge_dispatch<T>(sk, static_cast<unsigned char*>(own), (T*)out, rows, nparts,
                                                     world, p, st))
+}
+
+int launch_peer_fold(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t ncols_shard,
+                     int64_t srow, int64_t chunk, int64_t nparts, void* const* peers, int world, int rank, void* own,
+                     void* out, cudaStream_t st) {
+    const int64_t es = dtype_size(dtype), V = 16 / es;
+    if (!aligned16(x) || (rows > 1 && (srow * es) % 16 != 0) || ncols_shard % V != 0 || chunk % V != 0) {
+        set_error("nb200_peer_fold: needs a contiguous, 16-byte aligned shard whose width and chunk are multiples of "
+                  "%lld elements", (long long)V);
+        return NB200_ERR_ARG;
+    }
+    const int64_t nlocal = (ncols_shard + chunk - 1) / chunk;
+    if (nlocal > nparts) {
+        set_error("nb200_peer_fold: the shard has %lld chunks, more than the exchange's %lld parts per rank",
+                  (long long)nlocal, (long long)nparts);
+        return NB200_ERR_ARG;
+    }
+    PeerPtrs pp{};
+    for (int r = 0; r < world; ++r) pp.p[r] = static_cast<unsigned char*>(peers[r]);
+    const LdgSpan pl{rows, srow, 0, ncols_shard, chunk, nlocal, rows * nlocal, 0};
+    NB200_DTYPE_CASES(dtype, peer_fold_dispatch<T>(sk, (const T*)x, pl, nparts, pp, world, rank,
+                                                   static_cast<unsigned char*>(own), (T*)out, p, st))
 }
 
 int peer_fault_take(unsigned int* bits) {

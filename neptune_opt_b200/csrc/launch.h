@@ -24,10 +24,25 @@ int launch_partial(int sk, const Params& p, const void* x, int dtype, int64_t ro
 int launch_merge(int sk, const Params& p, const nb200_state* states, int64_t rows, int64_t nparts,
                  int64_t rs, int64_t ps, void* out, int dtype, cudaStream_t st);
 
+// Few, very wide rows in one launch: a thread-block cluster of csize CTAs per row whose states
+// (fold) or partial sums of squares (RMSNorm) meet through distributed shared memory
+// (rows_ldg.cu). x, gamma, y 16-byte aligned, contiguous rows whose byte length and stride are
+// 16-byte multiples. csize 0 picks the cluster size. Return 1 when launched, 0 when not taken,
+// negative on error.
+template <typename T>
+int launch_cluster_fold(int sk, const Params& p, const T* x, int64_t rows, int64_t ncols, int64_t srow, T* out,
+                        int csize, cudaStream_t st);
+template <typename T>
+int launch_cluster_rms(const T* x, const T* gamma, int64_t rows, int64_t ncols, int64_t srow, float eps, T* y,
+                       int csize, cudaStream_t st);
+
 // Column-sharded split plan across GPUs: chunk states exchanged through peer memory (fold.cu).
 int64_t peer_buffer_bytes(int64_t rows, int64_t world, int64_t nparts);
 int peer_max_world();
 int launch_peer_init(void* buffer, int64_t rows, int64_t nparts, int world, cudaStream_t st);
+int launch_peer_fold(int sk, const Params& p, const void* x, int dtype, int64_t rows, int64_t ncols_shard,
+                     int64_t srow, int64_t chunk, int64_t nparts, void* const* peers, int world, int rank, void* own,
+                     void* out, cudaStream_t st);
 int launch_peer_push(const nb200_state* states, int64_t rows, int64_t nlocal, int64_t nparts, void* const* peers,
                      int world, int rank, void* own, cudaStream_t st);
 int launch_peer_merge(int sk, const Params& p, void* own, int64_t rows, int64_t nparts, int world, void* out,

@@ -118,9 +118,41 @@ int rms_t(const T* x, const T* gamma, T* y, int64_t rows, int64_t ncols, int64_t
 
 }  // namespace
 
+// Few rows wider than 32 KB go to one thread-block cluster per row when x, gamma and y are
+// contiguous and 16-byte aligned (and the CTA ranges fit the kernel's registers).
+static int cluster_rms(const void* x, const void* gamma, int dtype, int64_t rows, int64_t ncols, int64_t srow,
+                       int64_t scol, int64_t sg, float eps, void* out, int csize, cudaStream_t st) {
+    const int64_t es = dtype_size(dtype);
+    if (scol != 1 || sg != 1 || !aligned16(x) || !aligned16(gamma) || !aligned16(out) || (ncols * es) % 16 != 0 ||
+        (srow * es) % 16 != 0)
+        return 0;
+    switch (dtype) {
+        case NB200_F32:
+            return launch_cluster_rms<float>((const float*)x, (const float*)gamma, rows, ncols, srow, eps, (float*)out,
+                                             csize, st);
+        case NB200_BF16:
+            return launch_cluster_rms<__nv_bfloat16>((const __nv_bfloat16*)x, (const __nv_bfloat16*)gamma, rows, ncols,
+                                                     srow, eps, (__nv_bfloat16*)out, csize, st);
+        case NB200_F16:
+            return launch_cluster_rms<__half>((const __half*)x, (const __half*)gamma, rows, ncols, srow, eps,
+                                              (__half*)out, csize, st);
+    }
+    return 0;
+}
+
 int launch_rms(const void* x, const void* gamma, int dtype, int64_t rows, int64_t ncols,
                int64_t srow, int64_t scol, int64_t sg, float eps, void* out,
                const nb200_launch* L, cudaStream_t st) {
+    const bool auto_cluster = rows >= 1 && rows <= (int64_t)sm_count() / 2 && ncols * (int64_t)dtype_size(dtype) > 32768;
+    if ((L && L->variant == NB200_VARIANT_CLUSTER) || ((!L || L->variant == NB200_VARIANT_AUTO) && auto_cluster)) {
+        const int rc = cluster_rms(x, gamma, dtype, rows, ncols, srow, scol, sg, eps, out, L ? L->stages : 0, st);
+        if (rc != 0) return rc < 0 ? rc : NB200_OK;
+        if (L && L->variant == NB200_VARIANT_CLUSTER) {
+            set_error("nb200_rms_norm: the cluster variant needs contiguous 16-byte-aligned x, gamma, y whose row "
+                      "ranges fit the kernel (at most 16 x 256 x 8 vectors per row)");
+            return NB200_ERR_ARG;
+        }
+    }
     if (!L || L->variant == NB200_VARIANT_AUTO || L->variant == NB200_VARIANT_STREAM) {
         const int rc = stream_rms(x, gamma, dtype, rows, ncols, srow, scol, sg, eps, out, L, st);
         if (rc != 0) return rc < 0 ? rc : NB200_OK;

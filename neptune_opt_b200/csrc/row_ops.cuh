@@ -238,17 +238,6 @@ template <typename T>
 int launch_ldg_span(int sk, const Params& p, const T* x, int64_t rows, int64_t cb, int64_t ns, int64_t srow,
                     int64_t cc, int64_t nparts, nb200_state* states, T* out, int finalize, cudaStream_t st);
 
-// Few, very wide rows in one launch: a thread-block cluster of csize CTAs per row whose states
-// (fold) or partial sums of squares (RMSNorm) meet through distributed shared memory (rows_ldg.cu).
-// x, gamma, y 16-byte aligned, contiguous rows whose byte length and stride are 16-byte multiples.
-// csize 0 picks the cluster size. Returns 1 when launched, 0 when not taken, negative on error.
-template <typename T>
-int launch_cluster_fold(int sk, const Params& p, const T* x, int64_t rows, int64_t ncols, int64_t srow, T* out,
-                        int csize, cudaStream_t st);
-template <typename T>
-int launch_cluster_rms(const T* x, const T* gamma, int64_t rows, int64_t ncols, int64_t srow, float eps, T* y,
-                       int csize, cudaStream_t st);
-
 // Whether the register-row kernel takes a row of `row_bytes` (16-byte multiple) by default.
 inline bool ldg_rows_eligible(uint32_t row_bytes) { return row_bytes >= 1024 && row_bytes <= 8192; }
 

@@ -13,10 +13,10 @@
 #include "fastmath.cuh"
 #include "launch.h"
 #include "row_ops.cuh"
+#include "span.cuh"
 
 namespace nb200 {
 
-constexpr int kLdgThreads = 128;
 
 // CTA size per Op: RMSNorm stages gamma (ncols values) into every CTA's shared memory, so fewer,
 // larger CTAs do less of that (measured 47.3 vs 48.9 us for bf16 [16384, 4096]); the others keep
@@ -125,119 +125,19 @@ int launch_ldg_rows(const T* x, int64_t rows, int64_t srow, const Op& op, uint32
     return launch_ldg_nv<T, Op, 16, false>(x, rows, srow, op, smem, st, what);
 }
 
-// ------------------------------------------------------------------ column spans
-// Split-plan chunks, and rows too long for one warp's registers: a warp folds one item (row,
-// column span) in sub-blocks of 32 x kSpanNV vectors (4 KB) loaded into registers at once. Per
-// lane a running fold state absorbs each sub-block; at the item's end the 32 lane states merge in
-// a fixed tree (lower lane on the left). Measured on B200 (bf16 [512, 262144], 16K-column
-// chunks): single 4 KB blocks with ~2x the resident warps beat double-buffered blocks, 54.9 us
-// against 70.8 us.
-constexpr int kSpanNV = 8;
-
-struct LdgSpan {
-    int64_t rows, srow, cb, ns, cc, nparts, nitems;
-    int finalize;
-};
-
-template <int NV, typename T>
-__device__ __forceinline__ void load_block(RegRow<NV>& b, const uint4* base, int v0, int nvec, int lane) {
-    b.lane = lane;
-    b.nv = min(32 * NV, nvec - v0);
-#pragma unroll
-    for (int k = 0; k < NV; ++k)
-        b.r[k] = (lane + 32 * k < b.nv) ? ld_stream(base + v0 + lane + 32 * k) : make_uint4(0u, 0u, 0u, 0u);
-}
-
-// 16-bit logsumexp sub-block: packed max with NaN propagation (a NaN or +inf in the block sends it
-// to the exact path), an online rescale of the lane's running sum when the block raises its max,
-// and 2^(x log2 e - m log2 e) on packed fp32 pairs. (Moving a share of the exponentials to an
-// FMA-pipe polynomial was measured slower here: this loop is bound by instruction issue, not by
-// the special-function unit.)
-template <typename T>
-__device__ __forceinline__ uint32_t max_nan2(uint32_t a, uint32_t b) {
-    uint32_t d;
-    if constexpr (sizeof(T) == 2 && Elem<T>::V == 8 && std::is_same<T, __half>::value)
-        asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    else
-        asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-template <typename T>
-__device__ __forceinline__ uint64_t widen2(uint32_t w) {
-    if constexpr (std::is_same<T, __half>::value) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
-        return f2(f.x, f.y);
-    } else {
-        return f2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
-    }
-}
-
-template <typename T>
-__device__ __forceinline__ void lse16_block(const RegRow<kSpanNV>& blk, St& run, const Params& p) {
-    const uint32_t ninf = std::is_same<T, __half>::value ? 0xFC00FC00u : 0xFF80FF80u;
-    uint32_t mw[4] = {ninf, ninf, ninf, ninf};
-    blk.for_each([&](const uint4& u, int) {
-        mw[0] = max_nan2<T>(mw[0], u.x);
-        mw[1] = max_nan2<T>(mw[1], u.y);
-        mw[2] = max_nan2<T>(mw[2], u.z);
-        mw[3] = max_nan2<T>(mw[3], u.w);
-    });
-    const uint64_t m2 = widen2<T>(max_nan2<T>(max_nan2<T>(mw[0], mw[1]), max_nan2<T>(mw[2], mw[3])));
-    const float bm = fmaxf(f2lo(m2), f2hi(m2));
-    if (f2lo(m2) != f2lo(m2) || f2hi(m2) != f2hi(m2) || bm == NB200_INF) {  // NaN or +inf: exact status
-        run = merge_fast<NB200_LOGSUMEXP>(run, lane_state<NB200_LOGSUMEXP, T>(blk, p), p);
-        return;
-    }
-    if (bm == -NB200_INF) return;  // nothing above -inf (or no element) in this lane's part
-    if (!run.seen || bm > run.m) {
-        if (run.seen) run.acc *= fexp(run.m - bm);
-        run.m = bm;
-        run.seen = 1;
-    }
-    const float nm = -run.m * kLog2e;
-    const uint64_t l2e = f2(kLog2e, kLog2e), nm2 = f2(nm, nm);
-    uint64_t acc[2] = {0ull, 0ull};
-#pragma unroll
-    for (int k = 0; k < kSpanNV; ++k) {
-        if (blk.lane + 32 * k >= blk.nv) continue;
-        const uint32_t w[4] = {blk.r[k].x, blk.r[k].y, blk.r[k].z, blk.r[k].w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint64_t x = fma2(widen2<T>(w[i]), l2e, nm2);
-            acc[i & 1] = add2(acc[i & 1], f2(ex2_ftz(f2lo(x)), ex2_ftz(f2hi(x))));
-        }
-    }
-    const uint64_t a = add2(acc[0], acc[1]);
-    run.acc += f2lo(a) + f2hi(a);
-}
-
+// ------------------------------------------------------------------ column spans (span.cuh)
 template <int S, typename T>
 __global__ void __launch_bounds__(kLdgThreads) ldg_span_kernel(const T* __restrict__ x, LdgSpan pl, Params p,
                                                                nb200_state* __restrict__ states, T* __restrict__ out) {
     pdl_wait();
     pdl_trigger();
-    constexpr int V = Elem<T>::V;
-    constexpr bool kFast = S == NB200_LOGSUMEXP && sizeof(T) == 2;
     const int lane = threadIdx.x & 31;
     const int64_t gw = (int64_t)blockIdx.x * (kLdgThreads / 32) + (threadIdx.x >> 5);
     const int64_t GW = (int64_t)gridDim.x * (kLdgThreads / 32);
     for (int64_t item = gw; item < pl.nitems; item += GW) {
-        const int64_t row = item / pl.nparts, part = item - row * pl.nparts;
-        const int64_t lo = pl.cb + part * pl.cc, hi = min(lo + pl.cc, pl.cb + pl.ns);
-        const uint4* base = reinterpret_cast<const uint4*>(x + row * pl.srow + lo);
-        const int nvec = (int)((hi - lo) / V);
-        St run = empty_state();
-        for (int v0 = 0; v0 < nvec; v0 += 32 * kSpanNV) {
-            RegRow<kSpanNV> blk;
-            load_block<kSpanNV, T>(blk, base, v0, nvec, lane);
-            if constexpr (kFast)
-                lse16_block<T>(blk, run, p);
-            else
-                run = merge_fast<S>(run, lane_state<S, T>(blk, p), p);
-        }
-        const St w = warp_merge<S>(run, lane, p);
+        const St w = span_item_state<S, T>(x, pl, item, lane, p);
         if (lane == 0) {
-            if (pl.finalize) out[row] = Elem<T>::from_f(finalize<S>(w, p));
+            if (pl.finalize) out[item / pl.nparts] = Elem<T>::from_f(finalize<S>(w, p));
             else reinterpret_cast<float4*>(states)[item] =
                      make_float4(w.m, w.acc, __int_as_float(w.seen), __int_as_float(w.status));
         }
@@ -462,10 +362,10 @@ __global__ void __launch_bounds__(kClThreads) cluster_rms_kernel(const T* __rest
 }
 
 // Cluster size for `rows` rows: as many CTAs per row as keep every SM busy, at most 16 (8 when the
-// hardware cannot place 16-CTA clusters of this kernel), at least 2.
+// hardware cannot place 16-CTA clusters of these 256-thread kernels), at least 2.
 template <typename K>
 static int cluster_ctas(K kernel, int64_t rows) {
-    static std::atomic<int> max16{-1};
+    static std::atomic<int> max16{-1};  // one answer per kernel signature: a property of the device
     int m = max16.load(std::memory_order_relaxed);
     if (m < 0) {
         m = 0;
@@ -492,6 +392,11 @@ static int cluster_ctas(K kernel, int64_t rows) {
 
 template <typename K, typename... Args>
 static int launch_cluster(K kernel, int64_t rows, int csize, cudaStream_t st, const char* what, Args... args) {
+    if (csize > 8 && cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("%s: %d-CTA clusters are not available", what, csize);
+        return NB200_ERR_LAUNCH;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(rows * csize));
     cfg.blockDim = dim3(kClThreads);

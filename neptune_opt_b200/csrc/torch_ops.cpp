@@ -9,7 +9,8 @@
 //        int num_warps=0) -> Tensor
 //       params = [tiny, alpha, T, beta, N, eps]; plan 0 serial, 1 split (block-column chunks);
 //       serial launch from num_warps as the host launch policy maps (block, num_warps): 0 the
-//       library's own choice, 1 one warp per row, n > 1 one CTA of 32 n threads per row
+//       library's own choice, 1 one warp per row, 2..16 one CTA of 32 n threads per row, 32 one
+//       thread-block cluster per row
 //   softmax(Tensor x, int mode) -> (Tensor y, Tensor lse)           mode 0 softmax, 1 log_softmax
 //   l2_normalize(Tensor x) -> (Tensor y, Tensor norm)
 //   rms_norm(Tensor x, Tensor gamma, float eps) -> Tensor
@@ -137,8 +138,10 @@ const nb200_launch* serial_launch(int64_t num_warps, nb200_launch* storage) {
     if (num_warps <= 0) return nullptr;
     if (num_warps == 1) {
         *storage = nb200_launch{NB200_VARIANT_WARP_ROW, 0, 0, 0};
+    } else if (num_warps == 32) {
+        *storage = nb200_launch{NB200_VARIANT_CLUSTER, 0, 0, 0};
     } else {
-        TORCH_CHECK_VALUE(num_warps <= 16, "nb200.fold: num_warps must be in 0..16, got ", num_warps);
+        TORCH_CHECK_VALUE(num_warps <= 16, "nb200.fold: num_warps must be in 0..16 or 32, got ", num_warps);
         *storage = nb200_launch{NB200_VARIANT_CTA_ROW, (int32_t)(32 * num_warps), 0, 0};
     }
     return storage;

@@ -248,6 +248,48 @@ class PeerExchange:
                                             stream), "peer merge")
         return out
 
+    def fold(self, name, params, x_shard, ncols_total, chunk, out):
+        """The whole call in one launch (nb200_peer_fold): fold this rank's contiguous shard
+        x_shard [rows, width] in `chunk`-column chunks, store the states into every rank's buffer,
+        raise the flags, wait for everyone's and merge into out[rows]. Same result, bit for bit,
+        as the partial fold followed by `exchange_and_merge`."""
+        from neptune_opt_b200 import _lib
+        from neptune_opt_b200.skeletons import SKELETONS, checked_params
+        from neptune_opt_b200.template import _on_device, current_stream, dtype_code
+
+        if self.peers is None:
+            raise RuntimeError("the peer exchange is closed")
+        if self.faulted:
+            raise RuntimeError("the peer exchange faulted (a bounded wait ran out or a layout differed); "
+                               "close it on every rank and set up a new one")
+        rows, width = x_shard.shape
+        if rows != self.rows or -(-width // chunk) > self.nparts:
+            raise ValueError(f"shard [{rows}, {width}] in {chunk}-column chunks does not fit the exchange "
+                             f"({self.rows} rows, {self.nparts} parts per rank)")
+        if out.dim() != 1 or out.numel() != rows or not out.is_contiguous() or out.dtype != x_shard.dtype:
+            raise ValueError(f"out must be a contiguous [{rows}] tensor of the shard's dtype")
+        if x_shard.device != self.buffer.device or out.device != self.buffer.device:
+            raise ValueError(f"x_shard and out must be on the exchange's device {self.buffer.device}")
+        p = _lib.params_struct(checked_params(name, params))
+        with _on_device(x_shard.device):
+            _lib.check(self._lib.nb200_peer_fold(SKELETONS[name].id, ctypes.byref(p),
+                                                 ctypes.c_void_p(x_shard.data_ptr()), dtype_code(x_shard.dtype), rows,
+                                                 int(ncols_total), width, x_shard.stride(0), int(chunk), self.nparts,
+                                                 self.peers, self.world, self.rank,
+                                                 ctypes.c_void_p(self.buffer.data_ptr()),
+                                                 ctypes.c_void_p(out.data_ptr()),
+                                                 ctypes.c_void_p(current_stream(x_shard.device))), "peer fold")
+        return out
+
+    @staticmethod
+    def fold_eligible(x_shard, chunk) -> bool:
+        """Whether a shard can take the one-launch form: contiguous 16-byte aligned rows whose width,
+        stride and chunk are multiples of 16 bytes."""
+        es = x_shard.element_size()
+        return (x_shard.dim() == 2 and x_shard.stride(1) == 1 and x_shard.data_ptr() % 16 == 0
+                and (x_shard.shape[0] <= 1 or (x_shard.stride(0) * es) % 16 == 0)
+                and (x_shard.shape[1] * es) % 16 == 0 and (chunk * es) % 16 == 0)
+
     def close(self):
         """Unmap the peers' buffers (collective: no rank may still be writing into another's)."""
         import torch
@@ -264,7 +306,8 @@ class PeerExchange:
 
 
 def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: int = 16384, group=None,
-                       partial_fn=None, merge_fn=None, widths=None, exchange=None, check: bool = False):
+                       partial_fn=None, merge_fn=None, widths=None, exchange=None, check: bool = False,
+                       fused: bool = True):
     """Fold rows whose columns are sharded across the ranks of `group`, rank order = column order.
 
     Each rank passes its own [rows, width_r] block (the ranks' blocks concatenated along columns in
@@ -278,7 +321,9 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
     rank order) skips the width exchange -- and its host synchronisation -- when the caller knows
     the layout, as a steady-state loop does. With `exchange` (a PeerExchange whose slot width is the
     largest rank's chunk count) the states move through NVLink peer memory instead of an
-    all-gather; the result is the same bit for bit. The exchange's output starts as NaN, so a merge
+    all-gather; the result is the same bit for bit -- in one launch (`PeerExchange.fold`) when the
+    shard is contiguous and aligned and `fused` is set, else as a partial fold plus the exchange's
+    push and merge kernels. The exchange's output starts as NaN, so a merge
     whose bounded wait ran out leaves NaN rather than stale memory; `check=True` synchronises after
     the merge and raises if a wait ran out or a layout differed (marking the exchange unusable).
     """
@@ -307,13 +352,16 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
         raise ValueError(f"column shards sum to {sum(all_widths)}, expected {ncols_total}")
     col_begin = sum(all_widths[:rank])
     max_parts = max(-(-w // chunk) for w in all_widths)
-    local = partial_fn(name, params, x_shard, col_begin, ncols_total, chunk)
     if exchange is not None:
         if exchange.nparts != max_parts or exchange.world != world:
             raise ValueError(f"the exchange holds {exchange.nparts} parts per rank for {exchange.world} ranks; "
                              f"this layout needs {max_parts} for {world}")
         out = torch.full((rows,), float("nan"), dtype=x_shard.dtype, device=x_shard.device)
-        exchange.exchange_and_merge(name, params, local, out)
+        if fused and partial_fn is _cuda_partial and exchange.fold_eligible(x_shard, chunk):
+            exchange.fold(name, params, x_shard, ncols_total, chunk, out)
+        else:
+            local = partial_fn(name, params, x_shard, col_begin, ncols_total, chunk)
+            exchange.exchange_and_merge(name, params, local, out)
         if check:
             from neptune_opt_b200 import _lib
 
@@ -325,6 +373,7 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
                                    + ("a buffer's layout differs from the call's; " if bits & 8 else "")
                                    + "close the exchange on every rank and set up a new one")
         return out
+    local = partial_fn(name, params, x_shard, col_begin, ncols_total, chunk)
     if local.shape[1] < max_parts:  # pad with empty (seen = 0) states
         pad = torch.zeros(rows, max_parts - local.shape[1], 4, dtype=local.dtype, device=local.device)
         pad[..., 0] = torch.tensor(float("-inf")).view(torch.int32) if local.dtype == torch.int32 else 0

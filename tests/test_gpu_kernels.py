@@ -52,6 +52,20 @@ def _oracle_rows(x):
     return x.float().reshape(-1, x.shape[-1]).cpu().numpy()
 
 
+def _sum_floor(name, rows, params):
+    """Cancellation floor of the signed-sum skeletons (linear_attn: terms x / max|x|; decay_renorm:
+    x / (N + max|x|)): 2^-19 sqrt(sum t^2) per row. The rounding errors of an fp32 sum of N such
+    terms form a random walk of about 2^-24 sqrt(log2 N) sqrt(sum t^2) in any summation order, so a
+    result that cancels to near zero is compared at that scale (the floor is ~8 times it), not
+    relative to itself. Other skeletons sum terms of one sign: no floor."""
+    if name not in ("linear_attn", "decay_renorm"):
+        return 0.0
+    a = np.asarray(rows, np.float64)
+    den = np.abs(a).max(axis=1) + (params.get("N", 0.0) if name == "decay_renorm" else 0.0)
+    t = a / np.maximum(den, 1e-30)[:, None]
+    return float(np.max(np.sqrt((t * t).sum(axis=1)))) * 2.0 ** -19
+
+
 def _scale(ref):
     fin = np.isfinite(ref)
     return float(np.max(np.abs(ref[fin]))) if fin.any() else 0.0
@@ -513,3 +527,107 @@ def test_long_length_vectors_build_spans_bit_exactly(oracle_mod):
         want, wst = oracle_mod.segment_spans(lengths.numpy(), False, False, T)
         got, gst = run(view, T, False, L.INDEX_CODES["int32"])
         assert np.array_equal(got, want) and gst == wst, f"{nseg} strided int32"
+
+
+def test_cluster_rows_fold_matches_oracle(oracle_mod):
+    """Few, very wide rows: one thread-block cluster per row, CTA states merged through distributed
+    shared memory. AUTO takes it for <= 74 rows wider than 32 KB; an explicit cluster launch forces
+    2, 8 or 16 CTAs per row; nonfinite rows keep the log family's status semantics; rows the
+    cluster kernel cannot take (strided) are refused by an explicit launch and folded by AUTO."""
+    import torch
+
+    import neptune_opt_b200 as NB
+    import neptune_opt_b200._lib as L
+
+    lib = L.load()
+    gen = torch.Generator().manual_seed(53)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def launch(name, params, x, csize):
+        p = L.params_struct(params)
+        out = torch.full((x.shape[0],), float("nan"), dtype=x.dtype, device="cuda")
+        forced = L.launch_struct(L.VARIANT_CLUSTER, 0, 0, csize)
+        rc = lib.nb200_fold(NB.SKELETONS[name].id, ctypes.byref(p), ctypes.c_void_p(x.data_ptr()),
+                            DTYPES.index(str(x.dtype)[6:]), x.shape[0], x.shape[1], x.stride(0), 1,
+                            ctypes.c_void_p(out.data_ptr()), ctypes.byref(forced), stream)
+        return rc, out
+
+    names = ("logsumexp", "lse_biased", "lse_scaled", "softcap_lse", "stable_l2", "linear_attn", "decay_renorm",
+             "sumsq_div", "rmsnorm_max")
+    for dtype in DTYPES:
+        for shape in ((1, 262144), (3, 70000), (8, 65536), (74, 40000)):
+            x = (torch.randn(*shape, generator=gen) * 3).to(_t(dtype)).cuda()
+            rows = _oracle_rows(x)
+            for name in names:
+                params = {**NB.param_defaults(name), **TEST_PARAMS.get(name, {})}
+                ref = oracle_mod.fold(name, rows, params)
+                atol = max(1e-6 * (1 + _scale(ref)), _sum_floor(name, rows, params))
+                assert_close_dtype(NB.run(name, x, **params).float().cpu().numpy(), ref, dtype, atol32=atol)
+                if shape[0] <= 8 and name in ("logsumexp", "stable_l2", "rmsnorm_max"):
+                    for csize in (2, 8, 16):
+                        rc, out = launch(name, params, x, csize)
+                        L.check(rc, f"cluster fold {csize}")
+                        assert_close_dtype(out.float().cpu().numpy(), ref, dtype, atol32=atol)
+    # nonfinite rows: the reference's log-family status (NaN wins, then +inf, -inf rows)
+    special = golden("fold.npz")["logsumexp|0|special|float32|x"]
+    wide = np.full((special.shape[0], 50000), -np.inf, np.float32)
+    wide[:, :special.shape[1]] = special
+    wide[:, 40000] = 0.5
+    wide[[1, 4], 40000] = -np.inf
+    for dtype in DTYPES:
+        x = torch.from_numpy(wide).to(_t(dtype)).cuda()
+        ref = oracle_mod.fold("logsumexp", x.float().cpu().numpy(), {"tiny": 0.0})
+        rc, out = launch("logsumexp", {"tiny": 0.0}, x, 8)
+        L.check(rc, "cluster fold special")
+        assert_nonfinite_equal(out.float().cpu().numpy(), ref)
+        assert_close_dtype(out.float().cpu().numpy(), ref, dtype)
+    # strided rows: refused by an explicit cluster launch, folded by AUTO's other paths
+    base = (torch.randn(4, 2 * 40000 + 2, generator=gen)).cuda()
+    x = base[:, 1:80001:2]
+    p = L.params_struct({"tiny": 0.0})
+    out = torch.empty(4, device="cuda")
+    forced = L.launch_struct(L.VARIANT_CLUSTER, 0, 0, 0)
+    rc = lib.nb200_fold(0, ctypes.byref(p), ctypes.c_void_p(x.data_ptr()), 0, 4, 40000, x.stride(0), x.stride(1),
+                        ctypes.c_void_p(out.data_ptr()), ctypes.byref(forced), stream)
+    assert rc == L.NB200_ERR_ARG
+    assert_close_dtype(NB.run("logsumexp", x).cpu().numpy(), oracle_mod.fold("logsumexp", _oracle_rows(x), {}),
+                       "float32")
+
+
+def test_cluster_rows_rms_norm_matches_oracle(oracle_mod):
+    """RMSNorm of few, very wide rows through one cluster per row (the partial sums of squares meet
+    in every CTA's shared memory), and the fallback when a row exceeds the cluster's registers."""
+    import torch
+
+    import neptune_opt_b200 as NB
+    import neptune_opt_b200._lib as L
+
+    lib = L.load()
+    gen = torch.Generator().manual_seed(59)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for dtype in DTYPES:
+        dt = _t(dtype)
+        for shape in ((1, 65536), (2, 131072), (7, 40000), (64, 16384 + 8)):
+            x = torch.randn(*shape, generator=gen).to(dt).cuda()
+            g = (1 + 0.1 * torch.randn(shape[1], generator=gen)).to(dt).cuda()
+            ref = oracle_mod.rms_norm(_oracle_rows(x), g.float().cpu().numpy(), 1e-6, dtype)
+            assert_rms_close(NB.run_rms_norm(x, g, eps=1e-6, plan="split").float().cpu().numpy(), ref, dtype)
+            for csize in (2, 16):
+                y = torch.full_like(x, float("nan"))
+                forced = L.launch_struct(L.VARIANT_CLUSTER, 0, 0, csize)
+                rc = lib.nb200_rms_norm(ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(g.data_ptr()),
+                                        DTYPES.index(dtype), shape[0], shape[1], shape[1], 1, 1, ctypes.c_double(1e-6),
+                                        ctypes.c_void_p(y.data_ptr()), ctypes.byref(forced), stream)
+                nvec = shape[1] * x.element_size() // 16
+                if -(-nvec // csize) > 256 * 8:
+                    # more vectors per CTA than its registers hold: refused, nothing written
+                    torch.cuda.synchronize()
+                    assert rc == L.NB200_ERR_ARG and torch.isnan(y).all()
+                    continue
+                L.check(rc, f"cluster rms {csize}")
+                assert_rms_close(y.float().cpu().numpy(), ref, dtype)
+    # wider than 16 CTAs x 256 threads x 8 vectors: AUTO falls back to the one-CTA-per-row kernel
+    x = torch.randn(1, 16 * 256 * 8 * 4 + 4, generator=gen).cuda()
+    g = torch.ones(x.shape[1], device="cuda")
+    ref = oracle_mod.rms_norm(_oracle_rows(x), g.float().cpu().numpy(), 1e-6, "float32")
+    assert_rms_close(NB.run_rms_norm(x, g, eps=1e-6, plan="split").float().cpu().numpy(), ref, "float32")

@@ -2,8 +2,9 @@
 
 Each rank folds its column shard of a bf16 [64, 100000] block into chunk states; they move either
 through one NCCL all-gather or through NVLink peer memory (PeerExchange: stores into every rank's
-buffer, a flag per rank, a merge that waits for all flags), and every rank merges them in ascending
-(rank, chunk) order. Both must equal, bit for bit, the single-GPU merge of the same states in the
+buffer, a flag per rank, a merge that waits for all flags -- in one cooperative launch, or as a
+partial fold plus push and merge kernels, alternating call by call), and every rank merges them in
+ascending (rank, chunk) order. Both must equal, bit for bit, the single-GPU merge of the same states in the
 same order, match the oracle within 1 bf16 ulp, agree with each other on inputs that change from
 call to call, and replay from a captured CUDA graph. Runs as two spawned processes; skipped with
 fewer than two GPUs.
@@ -56,11 +57,12 @@ def _rank_main(rank, world, port, result_path):
         ex = PeerExchange(ROWS, max(-(-w // CHUNK) for w in widths))
         try:
             peer_ok = []
-            for i in range(5):
+            for i in range(6):
+                # alternate the one-launch form and the partial + push + merge form: same protocol
                 xi = shard * (1.0 + 0.25 * i)
                 want = sharded_split_fold("logsumexp", xi, NCOLS, params={"tiny": 0.0}, chunk=CHUNK, widths=widths)
                 got = sharded_split_fold("logsumexp", xi, NCOLS, params={"tiny": 0.0}, chunk=CHUNK, widths=widths,
-                                         exchange=ex)
+                                         exchange=ex, fused=(i % 2 == 0))
                 peer_ok.append(bool(torch.equal(want, got)))
             first = sharded_split_fold("logsumexp", shard, NCOLS, params={"tiny": 0.0}, chunk=CHUNK, widths=widths,
                                        exchange=ex)

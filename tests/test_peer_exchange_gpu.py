@@ -2,9 +2,11 @@
 
 Two exchange buffers on the same device stand in for two ranks' buffers, so the kernels' own
 checks run without a second GPU:
-* world = 1: push + merge equal nb200_fold_merge of the same states, bit for bit;
+* world = 1: push + merge, and the one-launch nb200_peer_fold, equal nb200_fold_merge of the same
+  states, bit for bit, call after call (mixing the two forms);
 * a rank that never pushes: the merge's bounded wait for its flag runs out after about a second,
-  fault bit 2 (0x4) is reported once, and the NaN-filled output is left unwritten;
+  fault bit 2 (0x4) is reported once, and the NaN-filled output is left unwritten -- for the
+  merge kernel and for the one-launch form;
 * a buffer initialised for another layout: the push stores nothing into it and the merge reads
   nothing from it (fault bit 3, 0x8).
 No GPU is faulted or hung: the wait is bounded by the kernel and ends with a status the host reads.
@@ -88,13 +90,27 @@ def test_single_rank_exchange_equals_the_merge_kernel():
     p = L.params_struct({"tiny": 0.0})
     L.check(lib.nb200_fold_merge(NB.SKELETONS["logsumexp"].id, ctypes.byref(p), ctypes.c_void_p(states.data_ptr()),
                                  ROWS, nparts, nparts, 1, ctypes.c_void_p(want.data_ptr()), 0, _stream()), "merge")
-    for _ in range(3):  # consecutive calls walk the epochs and parities
+    for i in range(6):  # consecutive calls walk the epochs and parities, alternating the two forms
         out = torch.full((ROWS,), float("nan"), device="cuda")
-        L.check(_push(lib, states, ROWS, nparts, [buf], 0, buf), "push")
-        L.check(_merge(lib, L, buf, ROWS, nparts, 1, out), "peer merge")
+        if i % 2:
+            L.check(_fold(lib, L, x, nparts, [buf], 0, buf, out), "peer fold")
+        else:
+            L.check(_push(lib, states, ROWS, nparts, [buf], 0, buf), "push")
+            L.check(_merge(lib, L, buf, ROWS, nparts, 1, out), "peer merge")
         torch.cuda.synchronize()
-        assert torch.equal(out, want)
+        assert torch.equal(out, want), f"call {i}"
     assert L.stream_fault() == 0
+
+
+def _fold(lib, L, x, nparts, bufs, rank, own, out):
+    import neptune_opt_b200 as NB
+
+    p = L.params_struct({"tiny": 0.0})
+    peers = (ctypes.c_void_p * len(bufs))(*[b.data_ptr() for b in bufs])
+    rows, width = x.shape
+    return lib.nb200_peer_fold(NB.SKELETONS["logsumexp"].id, ctypes.byref(p), ctypes.c_void_p(x.data_ptr()), 0, rows,
+                               width, width, x.stride(0), CHUNK, nparts, peers, len(bufs), rank,
+                               ctypes.c_void_p(own.data_ptr()), ctypes.c_void_p(out.data_ptr()), _stream())
 
 
 def test_merge_wait_runs_out_when_a_rank_never_pushes():
@@ -120,6 +136,15 @@ def test_merge_wait_runs_out_when_a_rank_never_pushes():
     assert L.stream_fault() & 0x4, "the merge's wait for the missing rank's flag did not report running out"
     assert torch.isnan(out).all(), "the merge wrote an output although a rank's states never arrived"
     assert L.stream_fault() == 0, "the fault word was not cleared by reading it"
+    # the one-launch form: its in-kernel wait for "rank 1" runs out the same way
+    for b in (buf0, buf1):
+        _init(lib, L, b, ROWS, 2, nparts)
+    out = torch.full((ROWS,), float("nan"), device="cuda")
+    L.check(_fold(lib, L, x, nparts, [buf0, buf1], 0, buf0, out), "peer fold")
+    torch.cuda.synchronize()
+    assert L.stream_fault() & 0x4, "the one-launch form's wait did not report running out"
+    assert torch.isnan(out).all()
+    assert L.stream_fault() == 0
 
 
 def test_layout_mismatch_stores_and_reads_nothing():
