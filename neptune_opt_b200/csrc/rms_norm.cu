@@ -143,7 +143,7 @@ static int cluster_rms(const void* x, const void* gamma, int dtype, int64_t rows
 int launch_rms(const void* x, const void* gamma, int dtype, int64_t rows, int64_t ncols,
                int64_t srow, int64_t scol, int64_t sg, float eps, void* out,
                const nb200_launch* L, cudaStream_t st) {
-    const bool auto_cluster = rows >= 1 && rows <= (int64_t)sm_count() / 2 && ncols * (int64_t)dtype_size(dtype) > 32768;
+    const bool auto_cluster = rows >= 1 && rows <= 2 * (int64_t)sm_count() && ncols * (int64_t)dtype_size(dtype) > 32768;
     if ((L && L->variant == NB200_VARIANT_CLUSTER) || ((!L || L->variant == NB200_VARIANT_AUTO) && auto_cluster)) {
         const int rc = cluster_rms(x, gamma, dtype, rows, ncols, srow, scol, sg, eps, out, L ? L->stages : 0, st);
         if (rc != 0) return rc < 0 ? rc : NB200_OK;

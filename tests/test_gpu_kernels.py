@@ -531,7 +531,7 @@ def test_long_length_vectors_build_spans_bit_exactly(oracle_mod):
 
 def test_cluster_rows_fold_matches_oracle(oracle_mod):
     """Few, very wide rows: one thread-block cluster per row, CTA states merged through distributed
-    shared memory. AUTO takes it for <= 74 rows wider than 32 KB; an explicit cluster launch forces
+    shared memory. AUTO takes it for up to 296 rows wider than 32 KB; an explicit cluster launch forces
     2, 8 or 16 CTAs per row; nonfinite rows keep the log family's status semantics; rows the
     cluster kernel cannot take (strided) are refused by an explicit launch and folded by AUTO."""
     import torch
