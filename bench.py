@@ -401,12 +401,12 @@ def make_sharded_split(torch, NB, seed, dist, peer=False, fused=True):
         sharded_split_fold("logsumexp", xs[i % 2], ncols, params={"tiny": 0.0}, chunk=block, widths=[width] * n,
                            exchange=ex, fused=fused)
 
-    how = (("one cooperative launch: fold, stores into every rank's exchange buffer over NVLink, flags, wait, "
-            "merge" if fused else "partial fold, push kernel (stores + flag per rank), merge kernel (waits for "
+    how = (("two launches: fold storing into every rank's exchange buffer over NVLink, last CTA raises the flags; "
+            "merge waits for all flags" if fused else "partial fold, push kernel (stores + flag per rank), merge kernel (waits for "
             "all flags)") if peer else "states all-gathered over NCCL")
     name = "wide_logsumexp_split_sharded" + (("_peer" if fused else "_peer_3launch") if peer else "")
     return {"name": name, "step": step,
-            "bytes": rows * ncols * 2 + rows * 2, "rows": rows, "launches": (1 if fused else 3) if peer else 2,
+            "bytes": rows * ncols * 2 + rows * 2, "rows": rows, "launches": (2 if fused else 3) if peer else 2,
             "buffers": 2,
             "exchange": ex,
             "desc": f"logsumexp bf16 x[{rows},{ncols}] N(0,3^2), columns sharded over {n} GPUs ({width} each), "

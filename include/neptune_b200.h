@@ -210,12 +210,11 @@ int nb200_peer_push(const nb200_state* states, int64_t rows, int64_t nlocal, int
                     void* const* peers, int world, int rank, void* buffer, void* stream);
 int nb200_peer_merge(int skeleton, const nb200_params* params, void* buffer, int64_t rows,
                      int64_t nparts, int world, void* out, int dtype, void* stream);
-/* The same call in ONE launch (no counterpart in the reference): the partial fold of this rank's
+/* The same call in TWO launches (no counterpart in the reference): the partial fold of this rank's
  * column shard x[rows, ncols_shard] (contiguous rows, 16-byte aligned, row stride, width and
- * chunk_cols multiples of 16 bytes), the stores of its chunk states into every rank's buffer, the
- * flags and the merge of nb200_fold_partial + nb200_peer_push + nb200_peer_merge, in one
- * cooperative grid (every CTA resident, so the grid's in-kernel wait for the flags cannot keep its
- * own last CTA from running). ncols_total (all ranks' columns) sets the skeletons' 1/N as in
+ * chunk_cols multiples of 16 bytes) storing its chunk states straight into every rank's buffer,
+ * whose last CTA raises the flags (nb200_fold_partial + nb200_peer_push in one kernel), then the
+ * merge of nb200_peer_merge. ncols_total (all ranks' columns) sets the skeletons' 1/N as in
  * nb200_fold_partial. Same buffers, layout checks, fault bits, epochs, parities and protocol as
  * the push/merge pair (the two forms may be mixed, across ranks and across calls), and the same
  * result bit for bit. */

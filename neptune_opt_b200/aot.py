@@ -17,6 +17,11 @@ loaded into the process that runs the package (`load()`, or `torch.ops.load_libr
 The ops take their skeleton and parameters as arguments (one op per region kind) instead of
 baking them into the op name as the Python layer's per-key ops do: a C++ library registers its
 ops once at load, before any graph names a parameter set.
+
+`compile_package` compiles the packages with the library's C shims (`C_SHIMS`): the package calls
+`aoti_torch_cuda_fold(...)` and its siblings directly, instead of a boxed call through AOTInductor's
+proxy executor. The process that runs such a package must have loaded LIB with RTLD_GLOBAL (what
+`load()` does; a C++ host dlopens it with RTLD_GLOBAL) so the package resolves those symbols.
 """
 from __future__ import annotations
 
@@ -28,6 +33,7 @@ import tempfile
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "libneptune_b200_torch.so")
 SOURCE = os.path.join(HERE, "csrc", "torch_ops.cpp")
+EXPORTS = os.path.join(HERE, "csrc", "torch_ops.map")  # only the C shims are exported
 BUILD_DIR = os.path.join(HERE, "csrc", "_build", "torch_ops")
 
 _LOADED = False
@@ -39,27 +45,71 @@ def build(verbose: bool = False) -> str:
 
     os.makedirs(BUILD_DIR, exist_ok=True)
     cpp_extension.load(name="neptune_b200_torch", sources=[SOURCE], extra_cflags=["-O2", "-std=c++17"],
-                       extra_ldflags=["-ldl"], with_cuda=True, build_directory=BUILD_DIR,
-                       is_python_module=False, verbose=verbose)
+                       extra_ldflags=["-ldl", f"-Wl,--version-script={EXPORTS}"], with_cuda=True,
+                       build_directory=BUILD_DIR, is_python_module=False, verbose=verbose)
     shutil.copy2(os.path.join(BUILD_DIR, "neptune_b200_torch.so"), LIB)
+    import ctypes
+
+    # the copy cpp_extension.load just opened, made global: the C shims, for packages loaded here
+    ctypes.CDLL(os.path.join(BUILD_DIR, "neptune_b200_torch.so"), mode=ctypes.RTLD_GLOBAL)
     global _LOADED
     _LOADED = True  # cpp_extension.load registered the ops in this process
     return LIB
 
 
 def load() -> None:
-    """Register the nb200 ops in this process (fails loudly when the library is not built)."""
+    """Register the nb200 ops in this process (fails loudly when the library is not built). The
+    library is opened with RTLD_GLOBAL so that packages compiled with its C shims (`c_shims()`)
+    resolve them when they are loaded."""
     global _LOADED
     if _LOADED:
         return
+    import ctypes
+
     import torch
 
     if not os.path.exists(LIB):
         from neptune_opt_b200._lib import BackendUnavailable
 
         raise BackendUnavailable(f"{LIB} is not built; run neptune_opt_b200.aot.build()")
+    ctypes.CDLL(LIB, mode=ctypes.RTLD_GLOBAL)
     torch.ops.load_library(LIB)
     _LOADED = True
+
+
+# The C entry points of csrc/torch_ops.cpp, in AOTInductor's C-shim conventions.
+C_SHIMS = {
+    "fold": "AOTITorchError aoti_torch_cuda_fold(AtenTensorHandle x, int64_t skeleton, const double* params, "
+            "int64_t params_len_, int32_t keepdim, int64_t plan, int64_t block, int64_t num_warps, "
+            "AtenTensorHandle* ret0)",
+    "softmax": "AOTITorchError aoti_torch_cuda_softmax(AtenTensorHandle x, int64_t mode, AtenTensorHandle* ret0, "
+               "AtenTensorHandle* ret1)",
+    "l2_normalize": "AOTITorchError aoti_torch_cuda_l2_normalize(AtenTensorHandle x, AtenTensorHandle* ret0, "
+                    "AtenTensorHandle* ret1)",
+    "rms_norm": "AOTITorchError aoti_torch_cuda_rms_norm(AtenTensorHandle x, AtenTensorHandle gamma, double eps, "
+                "AtenTensorHandle* ret0)",
+    "segment_pool": "AOTITorchError aoti_torch_cuda_segment_pool(AtenTensorHandle data, AtenTensorHandle segments, "
+                    "int32_t offsets, int64_t reduce, double* initial, int32_t unsafe, AtenTensorHandle* ret0)",
+    "attention": "AOTITorchError aoti_torch_cuda_attention(AtenTensorHandle q, AtenTensorHandle k, AtenTensorHandle v, "
+                 "int32_t causal, double scale, AtenTensorHandle* ret0, AtenTensorHandle* ret1)",
+}
+
+
+def c_shims() -> dict:
+    """`aot_inductor.custom_ops_to_c_shims` for the nb200 ops: a package compiled with it calls the
+    library's C entry points directly instead of through the proxy executor's boxed call."""
+    import torch
+
+    load()
+    return {getattr(torch.ops.nb200, name).default: [decl] for name, decl in C_SHIMS.items()}
+
+
+def enable_c_shims() -> None:
+    """Make every later AOTInductor compilation in this process (the reference's compile_best
+    included) call the nb200 ops through their C shims."""
+    import torch._inductor.config as cfg
+
+    cfg.aot_inductor.custom_ops_to_c_shims = {**cfg.aot_inductor.custom_ops_to_c_shims, **c_shims()}
 
 
 def fold_params(name: str, params: dict | None = None) -> list:
@@ -110,10 +160,14 @@ def host_compiler() -> str:
     return configured
 
 
-def compile_package(exported, package_path: str | None = None) -> str:
-    """torch._inductor.aoti_compile_and_package with a host compiler that builds OpenMP code."""
+def compile_package(exported, package_path: str | None = None, *, shims: bool = True) -> str:
+    """torch._inductor.aoti_compile_and_package with a host compiler that builds OpenMP code and
+    (shims=True) the nb200 ops called through their C shims."""
     import torch
     import torch._inductor.config as cfg
 
-    with cfg.patch({"cpp.cxx": (None, host_compiler())}):
+    patch = {"cpp.cxx": (None, host_compiler())}
+    if shims:
+        patch["aot_inductor.custom_ops_to_c_shims"] = {**cfg.aot_inductor.custom_ops_to_c_shims, **c_shims()}
+    with cfg.patch(patch):
         return torch._inductor.aoti_compile_and_package(exported, package_path=package_path)

@@ -268,7 +268,7 @@ constexpr long long kPeerWaitCycles = 1ll << 31;
 constexpr unsigned int kPeerMagic = 0x4e425045u;  // "NBPE": written by peer_init_kernel
 struct PeerHeader {
     unsigned int ep;          // epoch of the last completed exchange on this rank
-    unsigned int arrive;      // CTAs of the one-launch exchange that have stored their states
+    unsigned int arrive;      // CTAs of the fused fold + push that have stored their states
     unsigned int merge_done;  // the same for the merge
     unsigned int pad;
     unsigned int flag[kMaxPeers];
@@ -390,22 +390,21 @@ peer_merge_kernel(unsigned char* own, T* __restrict__ out, int64_t rows, int64_t
     }
 }
 
-// One launch per call of the column-sharded split (nb200_peer_fold): the partial fold, the
-// exchange and the merge of the push / merge pair above in a single cooperative grid.
+// Two launches per call of the column-sharded split (nb200_peer_fold): the partial fold and the
+// push in one kernel, then peer_merge_kernel above.
 //   1. Each warp folds span items of this rank's shard (the split plan's span fold, so the states
 //      are bit-identical to nb200_fold_partial's) and lanes 0..world-1 store the item's state into
 //      slot `rank` of every rank's buffer (parts past this rank's chunk count are stored empty).
 //   2. Each CTA fences at system scope and counts itself in; the last CTA raises flag[rank] = e in
 //      every rank's buffer after another system-scope fence.
-//   3. Every CTA waits (bounded) until its own buffer holds every rank's flag for e, then the
-//      grid's warps merge the rows in ascending (rank, part) order; the last CTA records e.
-// The grid is launched cooperatively (all CTAs resident), so CTAs that wait in step 3 cannot keep
-// the last CTA of step 1 from running. Layouts are checked before any store (fault bit 3: nothing
-// stored, no flag raised); a wait that runs out sets fault bit 2 and leaves out unwritten.
+// No CTA waits here: the merge kernel, launched behind it, waits for the flags. Layouts are checked
+// before any store (fault bit 3: nothing stored, no flag raised).
 template <int S, typename T>
 __global__ void __launch_bounds__(kLdgThreads)
-peer_fold_kernel(const T* __restrict__ x, LdgSpan pl, int64_t slot_parts, Params p, PeerPtrs peers, int world,
-                 int rank, unsigned char* own, T* __restrict__ out) {
+peer_span_kernel(const T* __restrict__ x, LdgSpan pl, int64_t slot_parts, Params p, PeerPtrs peers, int world,
+                 int rank, unsigned char* own) {
+    pdl_wait();
+    pdl_trigger();
     PeerHeader* h = reinterpret_cast<PeerHeader*>(own);
     const int64_t rows = pl.rows;
     __shared__ int layout_ok;
@@ -443,33 +442,6 @@ peer_fold_kernel(const T* __restrict__ x, LdgSpan pl, int64_t slot_parts, Params
             unsigned int* f = &reinterpret_cast<PeerHeader*>(peers.p[r])->flag[rank];
             asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
         }
-    }
-    bool ok = true;
-    if (threadIdx.x < world) {
-        const long long t0 = clock64();
-        for (unsigned int it = 0;; ++it) {
-            unsigned int f;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(&h->flag[threadIdx.x]) : "memory");
-            if ((int)(f - e) >= 0) break;
-            if ((it & 63u) == 63u && clock64() - t0 > kPeerWaitCycles) {
-                ok = false;
-                atomicOr(&g_peer_fault, 4u);
-                break;
-            }
-        }
-    }
-    if (__syncthreads_and(ok)) {
-        const int64_t total = (int64_t)world * slot_parts;
-        const nb200_state* slots = reinterpret_cast<const nb200_state*>(own + kPeerHeaderBytes) + par * rows * total;
-        for (int64_t r = gw; r < rows; r += GW) {
-            const St s = merge_row<S, true>(slots + r * total, total, 1, lane, p);
-            if (lane == 0) out[r] = Elem<T>::from_f(finalize<S>(s, p));
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0 && atomicAdd(&h->merge_done, 1u) == gridDim.x - 1) {
-        atomicExch(&h->merge_done, 0u);
-        atomicExch(&h->ep, e);
     }
 }
 
@@ -679,28 +651,15 @@ int peer_fold_dispatch(int sk, const T* x, const LdgSpan& pl, int64_t slot_parts
     auto go = [&](auto k) {
         int occ = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kLdgThreads, 0) != cudaSuccess || occ < 1) occ = 1;
-        const int64_t warps = std::max(pl.rows * slot_parts, pl.rows);
+        const int64_t warps = std::max<int64_t>(pl.rows * slot_parts, 1);
         const int g = (int)std::max<int64_t>(1, std::min<int64_t>((warps + 3) / 4, (int64_t)sm_count() * occ));
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)g);
-        cfg.blockDim = dim3(kLdgThreads);
-        cfg.stream = st;
-        cudaLaunchAttribute at[1];
-        at[0].id = cudaLaunchAttributeCooperative;
-        at[0].val.cooperative = 1;
-        cfg.attrs = at;
-        cfg.numAttrs = 1;
-        const cudaError_t e = cudaLaunchKernelEx(&cfg, k, x, pl, slot_parts, p, pp, world, rank, own, out);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            set_error("nb200_peer_fold: cooperative launch failed: %s", cudaGetErrorString(e));
-            return (int)NB200_ERR_LAUNCH;
-        }
+        launch_pdl(k, (unsigned)g, kLdgThreads, 0, st, x, pl, slot_parts, p, pp, world, rank, own);
         count_launch();
-        return finish_launch("nb200_peer_fold");
+        const int rc = finish_launch("nb200_peer_fold");
+        return rc ? rc : peer_merge_dispatch<T>(sk, own, out, pl.rows, slot_parts, world, p, st);
     };
     switch (sk) {
-#define X(S) case S: return go(peer_fold_kernel<S, T>);
+#define X(S) case S: return go(peer_span_kernel<S, T>);
         NB200_SPLIT_SKELETONS(X)
 #undef X
     }

@@ -1,4 +1,4 @@
-// The column-span fold shared by the split plan's span kernel (rows_ldg.cu) and the one-launch
+// The column-span fold shared by the split plan's span kernel (rows_ldg.cu) and the fused
 // exchange of the column-sharded split across GPUs (fold.cu): a warp folds one item (row, column
 // span) in sub-blocks of 32 x kSpanNV vectors (4 KB) loaded into registers at once. Per lane a
 // running fold state absorbs each sub-block; at the item's end the 32 lane states merge in a fixed

@@ -28,6 +28,7 @@
 #include <ATen/ATen.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
+#include <torch/csrc/inductor/aoti_torch/utils.h>
 #include <torch/library.h>
 
 #include <cstring>
@@ -348,6 +349,67 @@ std::tuple<at::Tensor, at::Tensor> attention_meta(const at::Tensor& q, const at:
 }
 
 }  // namespace
+
+// ------------------------------------------------------------------ AOTInductor C shims
+// Direct C entry points for AOTInductor packages (torch._inductor.config.aot_inductor.
+// custom_ops_to_c_shims): a package compiled with them calls these functions instead of going
+// through the proxy executor's boxed dispatcher call, which costs microseconds per region call.
+// Argument conventions are AOTInductor's generated C shims': tensors as AtenTensorHandle, int as
+// int64_t, bool as int32_t, float as double, float? as double* (nullptr = None), float[] as pointer
+// + length, results as AtenTensorHandle* out-parameters. The process that runs such a package
+// must make these symbols visible (load this library with RTLD_GLOBAL, as aot.load() does).
+namespace {
+at::Tensor& tensor_of(AtenTensorHandle h) { return *torch::aot_inductor::tensor_handle_to_tensor_pointer(h); }
+}  // namespace
+
+extern "C" {
+AOTITorchError aoti_torch_cuda_fold(AtenTensorHandle x, int64_t skeleton, const double* params, int64_t params_len_,
+                                    int32_t keepdim, int64_t plan, int64_t block, int64_t num_warps,
+                                    AtenTensorHandle* ret0) {
+    AOTI_TORCH_CONVERT_EXCEPTION_TO_ERROR_CODE({
+        *ret0 = torch::aot_inductor::new_tensor_handle(fold_cuda(tensor_of(x), skeleton,
+                                                                 at::ArrayRef<double>(params, params_len_),
+                                                                 keepdim != 0, plan, block, num_warps));
+    });
+}
+AOTITorchError aoti_torch_cuda_softmax(AtenTensorHandle x, int64_t mode, AtenTensorHandle* ret0,
+                                       AtenTensorHandle* ret1) {
+    AOTI_TORCH_CONVERT_EXCEPTION_TO_ERROR_CODE({
+        auto r = softmax_cuda(tensor_of(x), mode);
+        *ret0 = torch::aot_inductor::new_tensor_handle(std::move(std::get<0>(r)));
+        *ret1 = torch::aot_inductor::new_tensor_handle(std::move(std::get<1>(r)));
+    });
+}
+AOTITorchError aoti_torch_cuda_l2_normalize(AtenTensorHandle x, AtenTensorHandle* ret0, AtenTensorHandle* ret1) {
+    AOTI_TORCH_CONVERT_EXCEPTION_TO_ERROR_CODE({
+        auto r = l2_cuda(tensor_of(x));
+        *ret0 = torch::aot_inductor::new_tensor_handle(std::move(std::get<0>(r)));
+        *ret1 = torch::aot_inductor::new_tensor_handle(std::move(std::get<1>(r)));
+    });
+}
+AOTITorchError aoti_torch_cuda_rms_norm(AtenTensorHandle x, AtenTensorHandle gamma, double eps,
+                                        AtenTensorHandle* ret0) {
+    AOTI_TORCH_CONVERT_EXCEPTION_TO_ERROR_CODE({
+        *ret0 = torch::aot_inductor::new_tensor_handle(rms_cuda(tensor_of(x), tensor_of(gamma), eps));
+    });
+}
+AOTITorchError aoti_torch_cuda_segment_pool(AtenTensorHandle data, AtenTensorHandle segments, int32_t offsets,
+                                            int64_t reduce, double* initial, int32_t unsafe, AtenTensorHandle* ret0) {
+    AOTI_TORCH_CONVERT_EXCEPTION_TO_ERROR_CODE({
+        const std::optional<double> init = initial ? std::optional<double>(*initial) : std::nullopt;
+        *ret0 = torch::aot_inductor::new_tensor_handle(
+            segment_cuda(tensor_of(data), tensor_of(segments), offsets != 0, reduce, init, unsafe != 0));
+    });
+}
+AOTITorchError aoti_torch_cuda_attention(AtenTensorHandle q, AtenTensorHandle k, AtenTensorHandle v, int32_t causal,
+                                         double scale, AtenTensorHandle* ret0, AtenTensorHandle* ret1) {
+    AOTI_TORCH_CONVERT_EXCEPTION_TO_ERROR_CODE({
+        auto r = attention_cuda(tensor_of(q), tensor_of(k), tensor_of(v), causal != 0, scale);
+        *ret0 = torch::aot_inductor::new_tensor_handle(std::move(std::get<0>(r)));
+        *ret1 = torch::aot_inductor::new_tensor_handle(std::move(std::get<1>(r)));
+    });
+}
+}  // extern "C"
 
 TORCH_LIBRARY(nb200, m) {
     m.def("fold(Tensor x, int skeleton, float[] params, bool keepdim, int plan, int block, int num_warps=0) -> Tensor");

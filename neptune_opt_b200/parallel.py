@@ -249,10 +249,10 @@ class PeerExchange:
         return out
 
     def fold(self, name, params, x_shard, ncols_total, chunk, out):
-        """The whole call in one launch (nb200_peer_fold): fold this rank's contiguous shard
-        x_shard [rows, width] in `chunk`-column chunks, store the states into every rank's buffer,
-        raise the flags, wait for everyone's and merge into out[rows]. Same result, bit for bit,
-        as the partial fold followed by `exchange_and_merge`."""
+        """The whole call in two launches (nb200_peer_fold): fold this rank's contiguous shard
+        x_shard [rows, width] in `chunk`-column chunks storing the states straight into every rank's
+        buffer (its last CTA raises the flags), then wait for everyone's and merge into out[rows].
+        Same result, bit for bit, as the partial fold followed by `exchange_and_merge`."""
         from neptune_opt_b200 import _lib
         from neptune_opt_b200.skeletons import SKELETONS, checked_params
         from neptune_opt_b200.template import _on_device, current_stream, dtype_code
@@ -283,8 +283,8 @@ class PeerExchange:
 
     @staticmethod
     def fold_eligible(x_shard, chunk) -> bool:
-        """Whether a shard can take the one-launch form: contiguous 16-byte aligned rows whose width,
-        stride and chunk are multiples of 16 bytes."""
+        """Whether a shard can take the fused form (`fold`): contiguous 16-byte aligned rows whose
+        width, stride and chunk are multiples of 16 bytes."""
         es = x_shard.element_size()
         return (x_shard.dim() == 2 and x_shard.stride(1) == 1 and x_shard.data_ptr() % 16 == 0
                 and (x_shard.shape[0] <= 1 or (x_shard.stride(0) * es) % 16 == 0)
@@ -321,9 +321,9 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
     rank order) skips the width exchange -- and its host synchronisation -- when the caller knows
     the layout, as a steady-state loop does. With `exchange` (a PeerExchange whose slot width is the
     largest rank's chunk count) the states move through NVLink peer memory instead of an
-    all-gather; the result is the same bit for bit -- in one launch (`PeerExchange.fold`) when the
-    shard is contiguous and aligned and `fused` is set, else as a partial fold plus the exchange's
-    push and merge kernels. The exchange's output starts as NaN, so a merge
+    all-gather; the result is the same bit for bit -- in two launches (`PeerExchange.fold`: the fold
+    stores into the peers' buffers itself) when the shard is contiguous and aligned and `fused` is
+    set, else as a partial fold plus the exchange's push and merge kernels. The exchange's output starts as NaN, so a merge
     whose bounded wait ran out leaves NaN rather than stale memory; `check=True` synchronises after
     the merge and raises if a wait ran out or a layout differed (marking the exchange unusable).
     """

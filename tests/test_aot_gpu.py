@@ -99,7 +99,17 @@ def test_aoti_package_runs_the_regions(tmp_path):
     args = _inputs()
     eager = model(*args)
     ep = torch.export.export(model, args)
+    # through the proxy executor's boxed calls, and (below) through the library's C shims
+    boxed = torch._inductor.aoti_load_package(A.compile_package(ep, str(tmp_path / "boxed.pt2"), shims=False))
+    for i, (a, b) in enumerate(zip(boxed(*args), eager)):
+        assert torch.equal(a, b), f"output {i} of the boxed-call package differs from eager"
     pkg = A.compile_package(ep, str(tmp_path / "regions.pt2"))
+    import zipfile
+
+    wrapper = [n for n in zipfile.ZipFile(pkg).namelist() if n.endswith(".wrapper.cpp")]
+    if wrapper:  # the package's generated code calls the C shims directly
+        src = zipfile.ZipFile(pkg).read(wrapper[0]).decode()
+        assert "aoti_torch_cuda_fold(" in src and "aoti_torch_cuda_attention(" in src
     runner = torch._inductor.aoti_load_package(pkg)
     before = NB.launch_count()
     got = runner(*args)
@@ -113,6 +123,8 @@ def test_aoti_package_runs_the_regions(tmp_path):
     torch.save([t.cpu() for t in args], tmp_path / "args.pt")
     script = f"""
 import torch
+import ctypes
+ctypes.CDLL({os.path.join(ROOT, "neptune_opt_b200", "libneptune_b200_torch.so")!r}, mode=ctypes.RTLD_GLOBAL)
 torch.ops.load_library({os.path.join(ROOT, "neptune_opt_b200", "libneptune_b200_torch.so")!r})
 args = [t.cuda() for t in torch.load({str(tmp_path / "args.pt")!r})]
 runner = torch._inductor.aoti_load_package({str(pkg)!r})

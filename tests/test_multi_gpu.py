@@ -2,8 +2,8 @@
 
 Each rank folds its column shard of a bf16 [64, 100000] block into chunk states; they move either
 through one NCCL all-gather or through NVLink peer memory (PeerExchange: stores into every rank's
-buffer, a flag per rank, a merge that waits for all flags -- in one cooperative launch, or as a
-partial fold plus push and merge kernels, alternating call by call), and every rank merges them in
+buffer, a flag per rank, a merge that waits for all flags -- the fold storing into the buffers
+itself, or a partial fold plus push and merge kernels, alternating call by call), and every rank merges them in
 ascending (rank, chunk) order. Both must equal, bit for bit, the single-GPU merge of the same states in the
 same order, match the oracle within 1 bf16 ulp, agree with each other on inputs that change from
 call to call, and replay from a captured CUDA graph. Runs as two spawned processes; skipped with
@@ -58,7 +58,7 @@ def _rank_main(rank, world, port, result_path):
         try:
             peer_ok = []
             for i in range(6):
-                # alternate the one-launch form and the partial + push + merge form: same protocol
+                # alternate the fused form and the partial + push + merge form: same protocol
                 xi = shard * (1.0 + 0.25 * i)
                 want = sharded_split_fold("logsumexp", xi, NCOLS, params={"tiny": 0.0}, chunk=CHUNK, widths=widths)
                 got = sharded_split_fold("logsumexp", xi, NCOLS, params={"tiny": 0.0}, chunk=CHUNK, widths=widths,

@@ -2,11 +2,11 @@
 
 Two exchange buffers on the same device stand in for two ranks' buffers, so the kernels' own
 checks run without a second GPU:
-* world = 1: push + merge, and the one-launch nb200_peer_fold, equal nb200_fold_merge of the same
-  states, bit for bit, call after call (mixing the two forms);
+* world = 1: push + merge, and the fused nb200_peer_fold (fold storing into the buffers, then the
+  merge), equal nb200_fold_merge of the same states, bit for bit, call after call (mixing forms);
 * a rank that never pushes: the merge's bounded wait for its flag runs out after about a second,
-  fault bit 2 (0x4) is reported once, and the NaN-filled output is left unwritten -- for the
-  merge kernel and for the one-launch form;
+  fault bit 2 (0x4) is reported once, and the NaN-filled output is left unwritten -- after the push
+  kernel and after the fused form;
 * a buffer initialised for another layout: the push stores nothing into it and the merge reads
   nothing from it (fault bit 3, 0x8).
 No GPU is faulted or hung: the wait is bounded by the kernel and ends with a status the host reads.
@@ -136,13 +136,13 @@ def test_merge_wait_runs_out_when_a_rank_never_pushes():
     assert L.stream_fault() & 0x4, "the merge's wait for the missing rank's flag did not report running out"
     assert torch.isnan(out).all(), "the merge wrote an output although a rank's states never arrived"
     assert L.stream_fault() == 0, "the fault word was not cleared by reading it"
-    # the one-launch form: its in-kernel wait for "rank 1" runs out the same way
+    # the fused form: its merge's wait for "rank 1" runs out the same way
     for b in (buf0, buf1):
         _init(lib, L, b, ROWS, 2, nparts)
     out = torch.full((ROWS,), float("nan"), device="cuda")
     L.check(_fold(lib, L, x, nparts, [buf0, buf1], 0, buf0, out), "peer fold")
     torch.cuda.synchronize()
-    assert L.stream_fault() & 0x4, "the one-launch form's wait did not report running out"
+    assert L.stream_fault() & 0x4, "the fused form's wait did not report running out"
     assert torch.isnan(out).all()
     assert L.stream_fault() == 0
 

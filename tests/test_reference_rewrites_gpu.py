@@ -102,6 +102,8 @@ def test_rewritten_programs_package_and_run_without_python_ops(tmp_path):
     torch.cuda.synchronize()
     script = f"""
 import sys, torch
+import ctypes
+ctypes.CDLL({os.path.join(ROOT, "neptune_opt_b200", "libneptune_b200_torch.so")!r}, mode=ctypes.RTLD_GLOBAL)
 torch.ops.load_library({os.path.join(ROOT, "neptune_opt_b200", "libneptune_b200_torch.so")!r})
 for name in {[j[0] for j in jobs]!r}:
     args = [t.cuda() for t in torch.load({str(tmp_path)!r} + "/" + name + ".args.pt")]
@@ -145,6 +147,7 @@ binding.install(neptune_codegen)
 # its OpenMP wrapper code (environment set-up, as for any AOTInductor user of this image)
 import neptune_opt_b200.aot as A
 torch._inductor.config.cpp.cxx = (None, A.host_compiler())
+A.enable_c_shims()  # the packages call the nb200 ops through their C entry points
 # bf16 outputs: the reference's explicit ULP slack (the ATen graph and the kernel round the same
 # fp32 values; RMSNorm rounds twice)
 ULPS = {{"rms_norm_bf16": 2, "logsumexp_split_bf16": 1}}
