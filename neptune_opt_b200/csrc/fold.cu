@@ -284,6 +284,15 @@ static_assert(sizeof(PeerHeader) <= kPeerHeaderBytes, "peer header");
 struct PeerPtrs {
     unsigned char* p[kMaxPeers];  // every rank's exchange buffer as mapped in this process
 };
+// peers.p[i] for a thread-dependent i without indexing the parameter array (which would copy it to
+// local memory): an unrolled select.
+__device__ __forceinline__ unsigned char* peer_at(const PeerPtrs& peers, int i) {
+    unsigned char* q = nullptr;
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r)
+        if (i == r) q = peers.p[r];
+    return q;
+}
 
 __device__ __forceinline__ bool peer_layout_ok(const unsigned char* buf, int64_t rows, int64_t nparts, int world) {
     const volatile PeerHeader* h = reinterpret_cast<const volatile PeerHeader*>(buf);
@@ -320,7 +329,7 @@ peer_push_kernel(const nb200_state* __restrict__ states, int64_t rows, int64_t n
     const PeerHeader* h = reinterpret_cast<const PeerHeader*>(own);
     const unsigned int e = *reinterpret_cast<const volatile unsigned int*>(&h->ep) + 1u;
     const int64_t par = e & 1u, n = rows * nparts;
-    unsigned char* dst = peers.p[blockIdx.x];
+    unsigned char* dst = peer_at(peers, blockIdx.x);
     __shared__ int layout_ok;
     if (threadIdx.x == 0) {
         layout_ok = peer_layout_ok(own, rows, nparts, world) && peer_layout_ok(dst, rows, nparts, world);
@@ -336,9 +345,11 @@ peer_push_kernel(const nb200_state* __restrict__ states, int64_t rows, int64_t n
                                        : make_float4(-NB200_INF, 0.f, 0.f, 0.f);
         slots[((par * rows + row) * world + rank) * nparts + part] = v;
     }
-    __threadfence_system();
+    // One system-scope fence by the flagging thread: the barrier orders every thread's stores
+    // before it and the fence is cumulative, so they are visible before the flag is.
     __syncthreads();
     if (threadIdx.x == 0) {
+        __threadfence_system();
         unsigned int* f = &reinterpret_cast<PeerHeader*>(dst)->flag[rank];
         asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
     }
@@ -400,7 +411,7 @@ peer_merge_kernel(unsigned char* own, T* __restrict__ out, int64_t rows, int64_t
 // No CTA waits here: the merge kernel, launched behind it, waits for the flags. Layouts are checked
 // before any store (fault bit 3: nothing stored, no flag raised).
 template <int S, typename T>
-__global__ void __launch_bounds__(kLdgThreads)
+__global__ void __launch_bounds__(kLdgThreads, 6)
 peer_span_kernel(const T* __restrict__ x, LdgSpan pl, int64_t slot_parts, Params p, PeerPtrs peers, int world,
                  int rank, unsigned char* own) {
     pdl_wait();
@@ -410,7 +421,7 @@ peer_span_kernel(const T* __restrict__ x, LdgSpan pl, int64_t slot_parts, Params
     __shared__ int layout_ok;
     if (threadIdx.x == 0) layout_ok = 1;
     __syncthreads();
-    if (threadIdx.x < world && !peer_layout_ok(peers.p[threadIdx.x], rows, slot_parts, world)) layout_ok = 0;
+    if (threadIdx.x < world && !peer_layout_ok(peer_at(peers, threadIdx.x), rows, slot_parts, world)) layout_ok = 0;
     __syncthreads();
     if (!layout_ok) {
         if (threadIdx.x == 0) atomicOr(&g_peer_fault, 8u);
@@ -419,6 +430,8 @@ peer_span_kernel(const T* __restrict__ x, LdgSpan pl, int64_t slot_parts, Params
     const unsigned int e = *reinterpret_cast<volatile unsigned int*>(&h->ep) + 1u;
     const int64_t par = e & 1u;
     const int lane = threadIdx.x & 31;
+    // lane r < world stores into rank r's buffer
+    float4* mine = lane < world ? reinterpret_cast<float4*>(peer_at(peers, lane) + kPeerHeaderBytes) : nullptr;
     const int64_t gw = (int64_t)blockIdx.x * (kLdgThreads / 32) + (threadIdx.x >> 5);
     const int64_t GW = (int64_t)gridDim.x * (kLdgThreads / 32);
     const int64_t nitems = rows * slot_parts;
@@ -429,18 +442,23 @@ peer_span_kernel(const T* __restrict__ x, LdgSpan pl, int64_t slot_parts, Params
             const St w = span_item_state<S, T>(x, pl, row * pl.nparts + part, lane, p);
             v = make_float4(w.m, w.acc, __int_as_float(w.seen), __int_as_float(w.status));
         }
-        if (lane < world)
-            reinterpret_cast<float4*>(peers.p[lane] + kPeerHeaderBytes)[((par * rows + row) * world + rank) * slot_parts +
-                                                                        part] = v;
+        if (mine) mine[((par * rows + row) * world + rank) * slot_parts + part] = v;
     }
-    __threadfence_system();
+    // The CTA's stores reach the count through thread 0: the barrier orders them before its
+    // (cumulative) system-scope fence, the fence before its increment; the last CTA fences again
+    // after seeing every increment and then raises the flags.
     __syncthreads();
-    if (threadIdx.x == 0 && atomicAdd(&h->arrive, 1u) == gridDim.x - 1) {
-        atomicExch(&h->arrive, 0u);
+    if (threadIdx.x == 0) {
         __threadfence_system();
-        for (int r = 0; r < world; ++r) {
-            unsigned int* f = &reinterpret_cast<PeerHeader*>(peers.p[r])->flag[rank];
-            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
+        if (atomicAdd(&h->arrive, 1u) == gridDim.x - 1) {
+            atomicExch(&h->arrive, 0u);
+            __threadfence_system();
+#pragma unroll
+            for (int r = 0; r < kMaxPeers; ++r) {
+                if (r >= world) break;
+                unsigned int* f = &reinterpret_cast<PeerHeader*>(peers.p[r])->flag[rank];
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
+            }
         }
     }
 }

@@ -6,6 +6,8 @@
 //   RmsOp     RMSNorm with the reference's fp32 stages (emitters.py:576-595)
 #pragma once
 
+#include <type_traits>
+
 #include "stream.cuh"
 
 namespace nb200 {
@@ -103,6 +105,10 @@ struct FoldOp {
     }
 };
 
+// Row sources that hold the whole row in registers (the register-row kernel's full rows).
+template <class Src, class = void> struct HoldsRegisters : std::false_type {};
+template <class Src> struct HoldsRegisters<Src, std::void_t<decltype(Src::kRegisters)>> : std::true_type {};
+
 template <typename T>
 struct SoftmaxOp {
     T* y;
@@ -110,8 +116,58 @@ struct SoftmaxOp {
     int64_t ncols;
     int nv, mode;
     __device__ __forceinline__ void prologue(unsigned char*) const {}
+
+    // softmax of an fp32 row held whole in registers: the exponentials of the sum pass are kept
+    // (over the row's own registers) and scaled by 1/sum for the output, so every element takes
+    // one exponential instead of two. Rows with a NaN or an infinity return false and take the
+    // general path below (exact status semantics).
+    template <class Src>
+    __device__ __forceinline__ bool softmax_in_registers(const Src& src, int64_t r, int lane) const {
+        constexpr int NV = sizeof(src.r) / sizeof(uint4);
+        float mx[4] = {-NB200_INF, -NB200_INF, -NB200_INF, -NB200_INF}, probe = 0.f;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            const uint4 u = src.r[k];
+            mx[0] = fmaxf(mx[0], __uint_as_float(u.x));
+            mx[1] = fmaxf(mx[1], __uint_as_float(u.y));
+            mx[2] = fmaxf(mx[2], __uint_as_float(u.z));
+            mx[3] = fmaxf(mx[3], __uint_as_float(u.w));
+            probe = fmaf(__uint_as_float(u.x) + __uint_as_float(u.y) + __uint_as_float(u.z) + __uint_as_float(u.w),
+                         0.f, probe);
+        }
+        if (!__all_sync(0xffffffffu, probe == 0.f)) return false;
+        const float m = warp_max(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
+        const float nm = -m * kLog2e;
+        uint4 e[NV];
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            const uint4 u = src.r[k];
+            const float e0 = ex2(fmaf(__uint_as_float(u.x), kLog2e, nm)), e1 = ex2(fmaf(__uint_as_float(u.y), kLog2e, nm));
+            const float e2 = ex2(fmaf(__uint_as_float(u.z), kLog2e, nm)), e3 = ex2(fmaf(__uint_as_float(u.w), kLog2e, nm));
+            acc[0] += e0;
+            acc[1] += e1;
+            acc[2] += e2;
+            acc[3] += e3;
+            e[k] = make_uint4(__float_as_uint(e0), __float_as_uint(e1), __float_as_uint(e2), __float_as_uint(e3));
+        }
+        const float s = warp_sum((acc[0] + acc[1]) + (acc[2] + acc[3]));
+        const float inv = 1.0f / s;
+        float* yrow = reinterpret_cast<float*>(y) + r * ncols;
+#pragma unroll
+        for (int k = 0; k < NV; ++k)
+            st_stream(yrow + (int64_t)(lane + 32 * k) * 4,
+                      make_uint4(__float_as_uint(__uint_as_float(e[k].x) * inv), __float_as_uint(__uint_as_float(e[k].y) * inv),
+                                 __float_as_uint(__uint_as_float(e[k].z) * inv), __float_as_uint(__uint_as_float(e[k].w) * inv)));
+        if (lse != nullptr && lane == 0) reinterpret_cast<float*>(lse)[r] = m + logf(s);
+        return true;
+    }
+
     template <class Src>
     __device__ __forceinline__ void row(const Src& src, int64_t r, int lane, const unsigned char*) const {
+        if constexpr (std::is_same<T, float>::value && HoldsRegisters<Src>::value) {
+            if (mode == 0 && softmax_in_registers(src, r, lane)) return;
+        }
         constexpr int V = Elem<T>::V;
         const Params p{0.f, 0.f, 1.f, 1.f, 0.f, 0.f, 0.f};
         const St s = row_state<NB200_LOGSUMEXP, T>(src, p);

@@ -39,6 +39,7 @@ template <int NV>
 struct RegRowFull {
     uint4 r[NV];
     static constexpr int nv = 32 * NV;
+    static constexpr bool kRegisters = true;  // the whole row, lane-strided, in r[]
     int lane;
     template <class F>
     __device__ __forceinline__ void for_each(F&& f) const {
