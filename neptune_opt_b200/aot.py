@@ -22,6 +22,8 @@ ops once at load, before any graph names a parameter set.
 `aoti_torch_cuda_fold(...)` and its siblings directly, instead of a boxed call through AOTInductor's
 proxy executor. The process that runs such a package must have loaded LIB with RTLD_GLOBAL (what
 `load()` does; a C++ host dlopens it with RTLD_GLOBAL) so the package resolves those symbols.
+It also runs `inductor_pass` (a float16/bfloat16 region's widening input cast and narrowing
+output cast folded into the kernel, which reads the 16-bit storage itself).
 """
 from __future__ import annotations
 
@@ -160,14 +162,20 @@ def host_compiler() -> str:
     return configured
 
 
-def compile_package(exported, package_path: str | None = None, *, shims: bool = True) -> str:
-    """torch._inductor.aoti_compile_and_package with a host compiler that builds OpenMP code and
-    (shims=True) the nb200 ops called through their C shims."""
+def compile_package(exported, package_path: str | None = None, *, shims: bool = True,
+                    fuse_casts: bool = True) -> str:
+    """torch._inductor.aoti_compile_and_package with a host compiler that builds OpenMP code,
+    (shims=True) the nb200 ops called through their C shims and (fuse_casts=True) the regions'
+    widening input casts folded into their kernels (`inductor_pass`)."""
     import torch
     import torch._inductor.config as cfg
 
     patch = {"cpp.cxx": (None, host_compiler())}
     if shims:
         patch["aot_inductor.custom_ops_to_c_shims"] = {**cfg.aot_inductor.custom_ops_to_c_shims, **c_shims()}
+    if fuse_casts and type(cfg.post_grad_custom_post_pass).__name__ != "CastFusion":
+        from neptune_opt_b200 import inductor_pass
+
+        patch["post_grad_custom_post_pass"] = inductor_pass.make_pass(cfg.post_grad_custom_post_pass)
     with cfg.patch(patch):
         return torch._inductor.aoti_compile_and_package(exported, package_path=package_path)

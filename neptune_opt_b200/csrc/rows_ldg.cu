@@ -128,6 +128,23 @@ int launch_ldg_rows(const T* x, int64_t rows, int64_t srow, const Op& op, uint32
 
 // ------------------------------------------------------------------ column spans (span.cuh)
 template <int S, typename T>
+__device__ __forceinline__ void span_store(const LdgSpan& pl, int64_t item, const St& w, const Params& p,
+                                           nb200_state* __restrict__ states, T* __restrict__ out) {
+    if (pl.finalize) out[item / pl.nparts] = Elem<T>::from_f(finalize<S>(w, p));
+    else reinterpret_cast<float4*>(states)[item] = make_float4(w.m, w.acc, __int_as_float(w.seen), __int_as_float(w.status));
+}
+
+// How a span kernel holds its items:
+//   kSpanStream   items of any width, folded in 4 KB sub-blocks (span_item_state);
+//   G = 1, 2, 4   every item fits 32 x kSpanNV / G vectors (chunks of at most 2048 / G 16-bit or
+//                 1024 / G fp32 columns): a warp loads G consecutive items into one 4 KB register
+//                 block and each is a resident row whose state is formed the way the reference
+//                 forms one chunk's (resident_items_state: the producer reduced across the warp
+//                 first, every term against it, one warp sum; no per-lane repair and no 32-state
+//                 merge tree), the G items' warp reductions interleaved.
+constexpr int kSpanStream = 0;
+
+template <int S, typename T, int G>
 __global__ void __launch_bounds__(kLdgThreads) ldg_span_kernel(const T* __restrict__ x, LdgSpan pl, Params p,
                                                                nb200_state* __restrict__ states, T* __restrict__ out) {
     pdl_wait();
@@ -135,12 +152,22 @@ __global__ void __launch_bounds__(kLdgThreads) ldg_span_kernel(const T* __restri
     const int lane = threadIdx.x & 31;
     const int64_t gw = (int64_t)blockIdx.x * (kLdgThreads / 32) + (threadIdx.x >> 5);
     const int64_t GW = (int64_t)gridDim.x * (kLdgThreads / 32);
-    for (int64_t item = gw; item < pl.nitems; item += GW) {
-        const St w = span_item_state<S, T>(x, pl, item, lane, p);
-        if (lane == 0) {
-            if (pl.finalize) out[item / pl.nparts] = Elem<T>::from_f(finalize<S>(w, p));
-            else reinterpret_cast<float4*>(states)[item] =
-                     make_float4(w.m, w.acc, __int_as_float(w.seen), __int_as_float(w.status));
+    if constexpr (G == kSpanStream) {
+        for (int64_t item = gw; item < pl.nitems; item += GW) {
+            const St w = span_item_state<S, T>(x, pl, item, lane, p);
+            if (lane == 0) span_store<S, T>(pl, item, w, p, states, out);
+        }
+    } else {
+        constexpr int NV = kSpanNV / G;
+        for (int64_t item = gw * G; item < pl.nitems; item += GW * G) {
+            RegRow<NV> blk[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) load_item<NV, T>(blk[g], x, pl, item + g, lane);
+            St w[G];
+            resident_items_state<S, T, NV, G>(blk, w, p);
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+                if (lane == g && item + g < pl.nitems) span_store<S, T>(pl, item + g, w[g], p, states, out);
         }
     }
 }
@@ -149,18 +176,28 @@ template <typename T>
 int launch_ldg_span(int sk, const Params& p, const T* x, int64_t rows, int64_t cb, int64_t ns, int64_t srow,
                     int64_t cc, int64_t nparts, nb200_state* states, T* out, int finalize, cudaStream_t st) {
     LdgSpan pl{rows, srow, cb, ns, cc, nparts, rows * nparts, finalize};
+    const int64_t nvec = cc / Elem<T>::V;  // vectors of the widest item
+    const int group = nvec <= 32 * kSpanNV / 4 ? 4 : nvec <= 32 * kSpanNV / 2 ? 2 : nvec <= 32 * kSpanNV ? 1
+                                                                                                      : kSpanStream;
     int rc = NB200_OK;
     auto go = [&](auto k) {
         int occ = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kLdgThreads, 0) != cudaSuccess || occ < 1) occ = 1;
-        const int64_t need = (pl.nitems + kLdgThreads / 32 - 1) / (kLdgThreads / 32);
+        const int64_t units = group > 1 ? (pl.nitems + group - 1) / group : pl.nitems;  // warp iterations
+        const int64_t need = (units + kLdgThreads / 32 - 1) / (kLdgThreads / 32);
         const int g = (int)std::min<int64_t>(need, (int64_t)sm_count() * occ);
         launch_pdl(k, (unsigned)std::max(g, 1), kLdgThreads, 0, st, x, pl, p, states, out);
         count_launch();
         rc = finish_launch(finalize ? "nb200_fold" : "nb200_fold_partial");
     };
     switch (sk) {
-#define X(S) case S: go(ldg_span_kernel<S, T>); break;
+#define X(S)                                                                                   \
+    case S:                                                                                    \
+        if (group == 4) go(ldg_span_kernel<S, T, 4>);                                          \
+        else if (group == 2) go(ldg_span_kernel<S, T, 2>);                                     \
+        else if (group == 1) go(ldg_span_kernel<S, T, 1>);                                     \
+        else go(ldg_span_kernel<S, T, kSpanStream>);                                           \
+        break;
         X(NB200_LOGSUMEXP) X(NB200_LSE_BIASED) X(NB200_LSE_SCALED) X(NB200_SOFTCAP_LSE) X(NB200_STABLE_L2)
         X(NB200_LINEAR_ATTN) X(NB200_DECAY_RENORM) X(NB200_SUMSQ_DIV) X(NB200_RMSNORM_MAX)
 #undef X

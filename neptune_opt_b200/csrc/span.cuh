@@ -54,8 +54,8 @@ __device__ __forceinline__ uint64_t widen2(uint32_t w) {
     }
 }
 
-template <typename T>
-__device__ __forceinline__ void lse16_block(const RegRow<kSpanNV>& blk, St& run, const Params& p) {
+template <typename T, int NV = kSpanNV>
+__device__ __forceinline__ void lse16_block(const RegRow<NV>& blk, St& run, const Params& p) {
     const uint32_t ninf = std::is_same<T, __half>::value ? 0xFC00FC00u : 0xFF80FF80u;
     uint32_t mw[4] = {ninf, ninf, ninf, ninf};
     blk.for_each([&](const uint4& u, int) {
@@ -80,7 +80,7 @@ __device__ __forceinline__ void lse16_block(const RegRow<kSpanNV>& blk, St& run,
     const uint64_t l2e = f2(kLog2e, kLog2e), nm2 = f2(nm, nm);
     uint64_t acc[2] = {0ull, 0ull};
 #pragma unroll
-    for (int k = 0; k < kSpanNV; ++k) {
+    for (int k = 0; k < NV; ++k) {
         if (blk.lane + 32 * k >= blk.nv) continue;
         const uint32_t w[4] = {blk.r[k].x, blk.r[k].y, blk.r[k].z, blk.r[k].w};
 #pragma unroll
@@ -93,6 +93,104 @@ __device__ __forceinline__ void lse16_block(const RegRow<kSpanNV>& blk, St& run,
     run.acc += f2lo(a) + f2hi(a);
 }
 
+
+// States of G whole 16-bit logsumexp items resident in `blk[g]`, each formed as row_state forms a
+// resident row (warp max first, every exponential against it, one warp sum; no repair) on packed
+// pairs: max.NaN on raw 16-bit pairs, exponent arguments and sums on fp32 pairs. The G items'
+// reductions interleave (one shuffle chain for all of them). A NaN or +inf anywhere in any of them
+// sends the warp to the exact lane-state merge for each item.
+template <typename T, int NV, int G>
+__device__ __forceinline__ void lse16_rows_state(const RegRow<NV> (&blk)[G], St (&out)[G], const Params& p) {
+    const uint32_t ninf = std::is_same<T, __half>::value ? 0xFC00FC00u : 0xFF80FF80u;
+    float m[G];
+    bool exact = false;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        uint32_t mw[4] = {ninf, ninf, ninf, ninf};
+        blk[g].for_each([&](const uint4& u, int) {
+            mw[0] = max_nan2<T>(mw[0], u.x);
+            mw[1] = max_nan2<T>(mw[1], u.y);
+            mw[2] = max_nan2<T>(mw[2], u.z);
+            mw[3] = max_nan2<T>(mw[3], u.w);
+        });
+        const uint64_t m2 = widen2<T>(max_nan2<T>(max_nan2<T>(mw[0], mw[1]), max_nan2<T>(mw[2], mw[3])));
+        m[g] = fmaxf(f2lo(m2), f2hi(m2));
+        exact |= f2lo(m2) != f2lo(m2) || f2hi(m2) != f2hi(m2) || m[g] == NB200_INF;
+    }
+    if (__any_sync(0xffffffffu, exact)) {
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+            out[g] = warp_merge<NB200_LOGSUMEXP>(lane_state<NB200_LOGSUMEXP, T>(blk[g], p), blk[g].lane, p);
+        return;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) m[g] = fmaxf(m[g], __shfl_xor_sync(0xffffffffu, m[g], o));
+    }
+    const uint64_t l2e = f2(kLog2e, kLog2e);
+    float sum[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        // an item with no element above -inf keeps an empty sum (its exponent arguments are not formed)
+        const float nm = m[g] == -NB200_INF ? 0.f : -m[g] * kLog2e;
+        const uint64_t nm2 = f2(nm, nm);
+        uint64_t acc[2] = {0ull, 0ull};
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            if (blk[g].lane + 32 * k >= blk[g].nv || m[g] == -NB200_INF) continue;
+            const uint32_t w[4] = {blk[g].r[k].x, blk[g].r[k].y, blk[g].r[k].z, blk[g].r[k].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint64_t x = fma2(widen2<T>(w[i]), l2e, nm2);
+                acc[i & 1] = add2(acc[i & 1], f2(ex2_ftz(f2lo(x)), ex2_ftz(f2hi(x))));
+            }
+        }
+        const uint64_t a = add2(acc[0], acc[1]);
+        sum[g] = f2lo(a) + f2hi(a);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) sum[g] += __shfl_xor_sync(0xffffffffu, sum[g], o);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+        out[g] = m[g] == -NB200_INF ? St{m[g], 0.f, 0, 0} : St{m[g], sum[g], 1, 0};
+}
+
+// States of G whole items resident in `blk[g]` (load_item), every lane returning the same states.
+template <int S, typename T, int NV, int G>
+__device__ __forceinline__ void resident_items_state(const RegRow<NV> (&blk)[G], St (&out)[G], const Params& p) {
+    if constexpr (S == NB200_LOGSUMEXP && sizeof(T) == 2) {
+        lse16_rows_state<T, NV, G>(blk, out, p);
+    } else {
+#pragma unroll
+        for (int g = 0; g < G; ++g) out[g] = row_state<S, T>(blk[g], p);
+    }
+}
+
+// Loads the vectors of span item `item` (row item / nparts, chunk item % nparts) into `blk`, which
+// must hold the whole item (the caller checks chunk <= 32 NV vectors); an item past the end loads
+// nothing.
+template <int NV, typename T>
+__device__ __forceinline__ void load_item(RegRow<NV>& blk, const T* __restrict__ x, const LdgSpan& pl, int64_t item,
+                                          int lane) {
+    constexpr int V = Elem<T>::V;
+    if (item >= pl.nitems) {
+        blk.lane = lane;
+        blk.nv = 0;
+        return;
+    }
+    int64_t row;
+    if (pl.nitems <= 0x7fffffff)  // 32-bit division: a 64-bit one is a long software sequence
+        row = (int64_t)((uint32_t)item / (uint32_t)pl.nparts);
+    else
+        row = item / pl.nparts;
+    const int64_t part = item - row * pl.nparts;
+    const int64_t lo = pl.cb + part * pl.cc, hi = min(lo + pl.cc, pl.cb + pl.ns);
+    load_block<NV, T>(blk, reinterpret_cast<const uint4*>(x + row * pl.srow + lo), 0, (int)((hi - lo) / V), lane);
+}
 
 // Warp-merged state of span item `item` (row item / nparts, chunk item % nparts). Every lane of the
 // warp must call it; every lane returns the same state.

@@ -1,0 +1,124 @@
+"""An Inductor post-grad pass that folds a region's widening input cast into the region's kernel.
+
+The reference's front end keeps casts outside every fusion region: for a float16/bfloat16 input
+its lowering widens the input to float32, fuses the float32 reduction, and narrows the result back
+to the input dtype afterwards (neptune_recognize/lowering.py:66-108). Compiled, that graph
+materialises a float32 copy of the whole input before the opaque region op reads it again: a
+bfloat16 [512, 262144] logsumexp moves 268 MB + 537 MB + 537 MB instead of 268 MB.
+
+The kernels here already read 16-bit storage and accumulate in float32 (every element widens
+exactly), and they round the float32 result to the storage dtype with round-to-nearest-even, which
+is what the trailing narrowing cast does. So
+
+    fold(convert(x16, float32)) -> convert(., dtype(x16))      becomes      fold(x16)
+
+when x16 is float16/bfloat16, the fold result has no other user than that narrowing cast, and
+the cast returns to x16's own dtype. The result is the same fold of the same values, rounded once
+in the same way; only the order in which a lane combines its elements can differ (16-byte loads
+hold eight 16-bit elements and four float32 ones), well inside the reduction's error bound.
+
+    from neptune_opt_b200 import inductor_pass
+    inductor_pass.enable()          # every later Inductor / AOTInductor compilation in the process
+"""
+from __future__ import annotations
+
+VERSION = "nb200-cast-fusion-1"
+
+
+def _dtype_of(node):
+    import torch
+
+    val = node.meta.get("val") if hasattr(node, "meta") else None
+    return val.dtype if isinstance(val, torch.Tensor) else None
+
+
+def _cast_source(node, dtype):
+    """x when `node` only converts x to `dtype` (prims.convert_element_type, or aten._to_copy /
+    aten.to with nothing but a dtype); else None."""
+    import torch
+
+    if getattr(node, "op", None) != "call_function":
+        return None
+    if node.target is torch.ops.prims.convert_element_type.default:
+        src, to = node.args[0], node.args[1] if len(node.args) > 1 else node.kwargs.get("dtype")
+        return src if to == dtype else None
+    if node.target is torch.ops.aten._to_copy.default:
+        if len(node.args) != 1 or set(node.kwargs) - {"dtype"} or node.kwargs.get("dtype") != dtype:
+            return None
+        return node.args[0]
+    return None
+
+
+def fuse_casts(graph) -> int:
+    """Rewrite every `narrow(fold(widen(x16)))` in `graph` (a torch.fx.Graph) to `fold(x16)`;
+    returns how many it rewrote."""
+    import torch
+
+    fold = torch.ops.nb200.fold.default
+    lowp = (torch.float16, torch.bfloat16)
+    rewritten = 0
+    for node in list(graph.nodes):
+        if node.op != "call_function" or node.target is not fold or _dtype_of(node) != torch.float32:
+            continue
+        src = _cast_source(node.args[0], torch.float32)
+        if src is None or _dtype_of(src) not in lowp:
+            continue
+        users = list(node.users)
+        if len(users) != 1 or _cast_source(users[0], _dtype_of(src)) is not node:
+            continue
+        narrow = users[0]
+        widen = node.args[0]
+        with graph.inserting_before(node):
+            fused = graph.call_function(fold, args=(src, *node.args[1:]), kwargs=dict(node.kwargs))
+        fused.meta = {**node.meta, "val": narrow.meta["val"]}
+        narrow.replace_all_uses_with(fused)
+        graph.erase_node(narrow)
+        graph.erase_node(node)
+        if not widen.users:
+            graph.erase_node(widen)
+        rewritten += 1
+    return rewritten
+
+
+def _pass_class():
+    from torch._inductor.custom_graph_pass import CustomGraphPass
+
+    class CastFusion(CustomGraphPass):
+        """`fuse_casts` as an Inductor post-grad pass (cached under VERSION)."""
+
+        def __init__(self, inner=None):
+            self.inner = inner
+            self.rewritten = 0
+
+        def __call__(self, graph):
+            if self.inner is not None:
+                self.inner(graph)
+            self.rewritten += fuse_casts(graph)
+
+        def uuid(self):
+            inner = self.inner.uuid() if hasattr(self.inner, "uuid") else repr(self.inner)
+            return f"{VERSION}:{inner}"
+
+    return CastFusion
+
+
+def make_pass(inner=None):
+    """A CustomGraphPass that runs `inner` (a pass already configured, or None) and then
+    `fuse_casts`."""
+    from neptune_opt_b200 import aot
+
+    aot.load()  # the pass names torch.ops.nb200.fold
+    return _pass_class()(inner)
+
+
+def enable():
+    """Install the pass as `post_grad_custom_post_pass` for every later Inductor compilation in
+    this process (the reference's compile_best packaging included), after any pass already there.
+    Idempotent; returns the installed pass."""
+    import torch._inductor.config as cfg
+
+    current = cfg.post_grad_custom_post_pass
+    if current is not None and type(current).__name__ == "CastFusion":
+        return current
+    cfg.post_grad_custom_post_pass = make_pass(current)
+    return cfg.post_grad_custom_post_pass

@@ -83,18 +83,30 @@ def test_rewritten_program_runs_and_matches_the_oracle(name, oracle_mod):
     _check_against_oracle(name, args, got, oracle_mod)
 
 
-def test_rewritten_programs_package_and_run_without_python_ops(tmp_path):
+def test_rewritten_programs_package_and_run_without_python_ops(tmp_path, oracle_mod):
     import torch
 
     import neptune_opt_b200.aot as A
     import rewrite_models
     from make_rewrites import load_case
 
+    from neptune_opt_b200.inductor_pass import fuse_casts
+
     jobs = []
     for name in CASES:
         ep, _case = load_case(name)
         args = rewrite_models.CASES[name][1]("cuda")
-        eager = ep.module()(*args)
+        # the package runs the graph with its 16-bit regions' casts folded into the kernels
+        # (compile_package's cast-fusion pass): run the same graph eagerly
+        eager_gm = ep.run_decompositions().module()
+        fused = fuse_casts(eager_gm.graph)
+        assert fused == (1 if name == "logsumexp_split_bf16" else 0), (name, fused)
+        eager_gm.recompile()
+        eager = eager_gm(*args)
+        if fused:
+            assert torch.equal(eager, torch.ops.nb200.fold(args[0], 0, [0.0, 0.0, 1.0, 1.0, 1.0, 1.0], False, 1,
+                                                           1024, 4))
+            _check_against_oracle(name, args, eager, oracle_mod)
         ep.example_inputs = (tuple(args), {})  # the fixtures keep none; AOTInductor compiles from these
         pkg = A.compile_package(ep, str(tmp_path / f"{name}.pt2"))
         torch.save([t.cpu() for t in args], tmp_path / f"{name}.args.pt")
@@ -148,6 +160,8 @@ binding.install(neptune_codegen)
 import neptune_opt_b200.aot as A
 torch._inductor.config.cpp.cxx = (None, A.host_compiler())
 A.enable_c_shims()  # the packages call the nb200 ops through their C entry points
+from neptune_opt_b200 import inductor_pass
+inductor_pass.enable()  # 16-bit regions read their storage directly (widen/narrow casts folded in)
 # bf16 outputs: the reference's explicit ULP slack (the ATen graph and the kernel round the same
 # fp32 values; RMSNorm rounds twice)
 ULPS = {{"rms_norm_bf16": 2, "logsumexp_split_bf16": 1}}
@@ -177,3 +191,53 @@ print(json.dumps(results))
         assert r["fused_package"], (name, r)  # compiled, loaded and matched the baseline's numbers
         assert r["launches"] > 0, (name, r)
         print(f"\n{name}: compile_best {r['reason']} (speedup {r['speedup']})")
+
+
+def test_compile_best_keeps_the_fusion_at_the_benchmark_configurations(tmp_path):
+    """The reference's compile_best (its export, apply, AOTInductor packaging, verification and
+    A/B timing gate, neptune_opt/ab.py:270-530) on the benchmark configurations: logsumexp fp32
+    [8192, 2048], RMSNorm bf16 [16384, 4096] and the split plan on bf16 [512, 262144]. The gate
+    keeps a fused package only when it is faster than Inductor's own compilation of the
+    unfused graph on that input."""
+    root = _reference_root()
+    if root is None:
+        pytest.skip("the reference is not installed under baseline/_ref")
+    code = f"""
+import json, sys
+sys.path[:0] = [{root!r}, {ROOT!r}, {GOLDEN!r}]
+import torch, neptune_codegen
+from neptune_opt.ab import compile_best
+from neptune_opt_b200 import binding, inductor_pass
+import neptune_opt_b200.aot as A
+import rewrite_models as RM
+binding.install(neptune_codegen)
+torch._inductor.config.cpp.cxx = (None, A.host_compiler())
+A.enable_c_shims()
+inductor_pass.enable()
+g = torch.Generator(device="cuda").manual_seed(7)
+def lse():
+    return (torch.randn(8192, 2048, device="cuda", generator=g) * 3.0,)
+def rms():
+    x = torch.randn(16384, 4096, device="cuda", generator=g).to(torch.bfloat16)
+    return (x, (1 + 0.1 * torch.randn(4096, device="cuda", generator=g)).to(torch.bfloat16))
+def split():
+    return ((torch.randn(512, 262144, device="cuda", generator=g) * 3.0).to(torch.bfloat16),)
+cases = {{
+    "logsumexp_f32_8192x2048": (RM.LogsumexpRows, lse, {{}}, {{}}),
+    "rms_norm_bf16_16384x4096": (RM.RmsNormGamma, rms, {{"capabilities": ("rms_norm",)}}, {{"max_ulps": 2}}),
+    "logsumexp_split_bf16_512x262144": (RM.LogsumexpRows, split, {{"plan": "split"}}, {{"max_ulps": 1}}),
+}}
+out = {{}}
+for name, (cls, build, kw, slack) in cases.items():
+    choice = compile_best(cls(), build(), package_dir={str(tmp_path)!r} + "/" + name, verbose=False,
+                          capabilities=kw.get("capabilities", ()), plans=(kw.get("plan", "serial"),), **slack)
+    out[name] = {{"used_fusion": bool(choice.used_fusion), "speedup": choice.speedup, "reason": choice.reason}}
+print(json.dumps(out))
+"""
+    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=1800)
+    assert res.returncode == 0, res.stderr[-3000:]
+    results = json.loads(res.stdout.strip().splitlines()[-1])
+    for name, r in results.items():
+        print(f"\n{name}: speedup {r['speedup']:.2f} ({r['reason']})")
+    for name, r in results.items():
+        assert r["used_fusion"], (name, r)
