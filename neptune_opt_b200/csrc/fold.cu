@@ -213,15 +213,25 @@ __device__ __forceinline__ St merge_row(const nb200_state* row, int64_t nparts, 
     St s = empty_state();
     const int64_t lo = (int64_t)lane * k;
     const int64_t hi = min(lo + k, nparts);
-    for (int64_t j = lo; j < hi; ++j) {
-        nb200_state b;
-        if constexpr (kL2) {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(row + j * pstride));
-            b = nb200_state{v.x, v.y, __float_as_int(v.z), __float_as_int(v.w)};
-        } else {
-            b = row[j * pstride];
+    constexpr int kBatch = 8;  // a lane's states are loaded kBatch at a time, then merged in order
+    const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;  // else 4-byte loads (caller's layout)
+    for (int64_t j0 = lo; j0 < hi; j0 += kBatch) {
+        float4 b[kBatch];
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u) {
+            if (j0 + u >= hi) continue;
+            const nb200_state* q = row + (j0 + u) * pstride;
+            if (vec) {
+                b[u] = kL2 ? __ldcg(reinterpret_cast<const float4*>(q)) : __ldg(reinterpret_cast<const float4*>(q));
+            } else {
+                const float* f = reinterpret_cast<const float*>(q);
+                b[u] = kL2 ? make_float4(__ldcg(f), __ldcg(f + 1), __ldcg(f + 2), __ldcg(f + 3))
+                           : make_float4(__ldg(f), __ldg(f + 1), __ldg(f + 2), __ldg(f + 3));
+            }
         }
-        s = merge<S>(s, St{b.m, b.acc, b.seen, b.status}, p);
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+            if (j0 + u < hi) s = merge<S>(s, St{b[u].x, b[u].y, __float_as_int(b[u].z), __float_as_int(b[u].w)}, p);
     }
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -231,7 +241,8 @@ __device__ __forceinline__ St merge_row(const nb200_state* row, int64_t nparts, 
     return s;
 }
 
-// One warp per row.
+// One warp per row, two rows per CTA: the few hundred rows of a split plan spread over every SM.
+constexpr int kMergeThreads = 64;
 template <int S, typename T>
 __global__ void __launch_bounds__(256)
 merge_kernel(const nb200_state* __restrict__ states, T* __restrict__ out, int64_t rows,
@@ -620,8 +631,8 @@ template <int S, typename T>
 int merge_t(const nb200_state* states, T* out, int64_t rows, int64_t nparts, int64_t rs, int64_t ps,
             const Params& p, cudaStream_t st) {
     auto k = merge_kernel<S, T>;
-    const int g = persistent_grid(k, 256, 0, (rows + 7) / 8, 0);
-    launch_pdl(k, g, 256, 0, st, states, out, rows, nparts, rs, ps, p);
+    const int g = persistent_grid(k, kMergeThreads, 0, (rows + kMergeThreads / 32 - 1) / (kMergeThreads / 32), 0);
+    launch_pdl(k, g, kMergeThreads, 0, st, states, out, rows, nparts, rs, ps, p);
     count_launch();
     return finish_launch("nb200_fold_merge");
 }
