@@ -378,8 +378,8 @@ def make_small(torch, NB, seed, kind):
 def make_sharded_split(torch, NB, seed, dist, peer=False, fused=True):
     """BASELINE config 3b across GPUs: the columns of bf16 [512, 262144] split into one shard per
     rank; each rank folds its shard into 16K-column chunk states, which move to every rank -- one
-    NCCL all-gather, or (peer=True) stores into every rank's exchange buffer over NVLink with a flag
-    per rank -- and every rank merges them in ascending (rank, chunk) order. Total work is fixed
+    NCCL all-gather, or (peer=True) epoch-tagged stores into every rank's exchange buffer over
+    NVLink -- and every rank merges them in ascending (rank, chunk) order. Total work is fixed
     (strong scaling)."""
     from neptune_opt_b200.parallel import PeerExchange, sharded_split_fold
 
@@ -401,9 +401,10 @@ def make_sharded_split(torch, NB, seed, dist, peer=False, fused=True):
         sharded_split_fold("logsumexp", xs[i % 2], ncols, params={"tiny": 0.0}, chunk=block, widths=[width] * n,
                            exchange=ex, fused=fused)
 
-    how = (("two launches: fold storing into every rank's exchange buffer over NVLink, last CTA raises the flags; "
-            "merge waits for all flags" if fused else "partial fold, push kernel (stores + flag per rank), merge kernel (waits for "
-            "all flags)") if peer else "states all-gathered over NCCL")
+    how = (("two launches: fold storing epoch-tagged states into every rank's exchange buffer over NVLink; "
+            "merge reads each state until it carries the call's epoch" if fused else "partial fold, push kernel "
+            "(epoch-tagged stores into every rank's buffer), merge kernel (reads each state until tagged)")
+           if peer else "states all-gathered over NCCL")
     name = "wide_logsumexp_split_sharded" + (("_peer" if fused else "_peer_3launch") if peer else "")
     return {"name": name, "step": step,
             "bytes": rows * ncols * 2 + rows * 2, "rows": rows, "launches": (2 if fused else 3) if peer else 2,

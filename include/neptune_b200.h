@@ -106,7 +106,7 @@ uint64_t nb200_launch_count(void);
 /* Reads and clears the fault bits of the kernels with device-side waits or checks (bit 0: a
  * bounded wait on a bulk copy in a streaming kernel ran out and the kernel stopped early; bit 1: a
  * bounded wait in the attention kernel ran out and its output was left unwritten; bit 2: the peer
- * merge's bounded wait for the ranks' flags ran out, output unwritten; bit 3: a peer push or merge
+ * merge's bounded wait for the ranks' states ran out, output unwritten; bit 3: a peer push or merge
  * found a buffer whose recorded layout differs from the call's, nothing stored or read).
  * Synchronous. No counterpart in the reference, whose Triton kernels have no device-side waits. */
 int nb200_stream_fault(uint32_t* bits);
@@ -185,16 +185,17 @@ int nb200_fold_merge(int skeleton, const nb200_params* params,
  * multi-GPU path): column shards' chunk states move through NVLink peer memory. Each rank owns an
  * exchange buffer of nb200_peer_buffer_bytes(rows, world, nparts) bytes (device memory, 256-byte
  * aligned, reused across calls), initialises it once with nb200_peer_init (which records the
- * (rows, world, nparts) layout in the buffer's header and clears its epoch and flags), and maps
+ * (rows, world, nparts) layout in the buffer's header, clears its epoch and zeroes its slots), and maps
  * every other rank's buffer with nb200_ipc_handle / nb200_ipc_open (CUDA IPC; the library only
  * maps, it allocates nothing). Every rank initialises before any rank's first push (a barrier
  * between them). Per call, in this order on one stream:
  *   nb200_fold_partial  -> states[rows][nlocal] of this rank's shard;
  *   nb200_peer_push     -> writes them into slot `rank` (nparts wide, parts past nlocal empty) of
- *                          every rank's buffer and raises this rank's flag there (peers[r] = rank
- *                          r's buffer as mapped here, peers[rank] = buffer);
- *   nb200_peer_merge    -> waits until every rank's flag has arrived (bounded: about a second, then
- *                          bit 2 of nb200_stream_fault and the output is left unwritten), merges
+ *                          every rank's buffer (peers[r] = rank r's buffer as mapped here,
+ *                          peers[rank] = buffer), each state tagged with the call's epoch inside
+ *                          its 16 bytes (no fence, no flag);
+ *   nb200_peer_merge    -> reads each state until it carries the call's epoch (bounded: about a
+ *                          second, then bit 2 of nb200_stream_fault and the row is left unwritten), merges
  *                          each row's world * nparts states in ascending (rank, part) order into
  *                          out[rows] -- the result of nb200_fold_merge on the gathered states.
  * Every rank makes the same calls in the same order with the same rows and nparts; a call's epoch
@@ -212,8 +213,8 @@ int nb200_peer_merge(int skeleton, const nb200_params* params, void* buffer, int
                      int64_t nparts, int world, void* out, int dtype, void* stream);
 /* The same call in TWO launches (no counterpart in the reference): the partial fold of this rank's
  * column shard x[rows, ncols_shard] (contiguous rows, 16-byte aligned, row stride, width and
- * chunk_cols multiples of 16 bytes) storing its chunk states straight into every rank's buffer,
- * whose last CTA raises the flags (nb200_fold_partial + nb200_peer_push in one kernel), then the
+ * chunk_cols multiples of 16 bytes) storing its tagged chunk states straight into every rank's
+ * buffer (nb200_fold_partial + nb200_peer_push in one kernel), then the
  * merge of nb200_peer_merge. ncols_total (all ranks' columns) sets the skeletons' 1/N as in
  * nb200_fold_partial. Same buffers, layout checks, fault bits, epochs, parities and protocol as
  * the push/merge pair (the two forms may be mixed, across ranks and across calls), and the same

@@ -261,17 +261,19 @@ merge_kernel(const nb200_state* __restrict__ states, T* __restrict__ out, int64_
 // ------------------------------------------------------------------ split plan across GPUs
 // The column-sharded split plan exchanges its chunk states through peer memory instead of a
 // collective. Each rank owns an exchange buffer, mapped into every other rank's address space:
-//   header   epoch of the last completed exchange, two completion counters, flag[r] = the last
-//            epoch rank r has delivered here;
-//   slots    two parities x [rows][world][nparts] states; call e uses parity e & 1.
-// Call e: peer_push_kernel writes this rank's states into slot `rank` of parity e & 1 in every
-// rank's buffer (stores over NVLink), one CTA per destination, each raising flag[rank] = e in its
-// destination after a system-scope fence. peer_merge_kernel waits until every flag has reached e (bounded),
-// merges each row's world * nparts states in ascending (rank, part) order -- the order of the
-// single-GPU split plan -- and its last CTA records e as completed. A rank can be at most one call
-// ahead of another (its next push follows its own merge, which needs everyone's flag), so two
-// parities keep a fast rank from overwriting states a slow one is still merging. The epoch lives
-// in device memory, so a captured CUDA graph replays correctly.
+//   header   epoch of the last completed exchange, a completion counter, the recorded layout;
+//   slots    two parities x [rows][world][nparts] tagged states; call e uses parity e & 1.
+// A slot carries its epoch inside the data (the split plan's states are 16 bytes): two 8-byte
+// words {m, e} and {acc, e << 5 | status << 1 | seen}, written with one 16-byte store whose two
+// 8-byte halves are each single-copy atomic. Call e: the fold (peer_span_kernel, or the partial
+// fold + peer_push_kernel) writes this rank's states into slot `rank` of parity e & 1 in every
+// rank's buffer (stores over NVLink, no fence, no flag); peer_merge_kernel reads each state until
+// both its words carry epoch e (bounded), merges each row's world * nparts states in ascending
+// (rank, part) order -- the order of the single-GPU split plan -- and its last CTA records e as
+// completed. A rank can be at most one call ahead of another (its next stores follow its own
+// merge, which needs everyone's states), so two parities keep a fast rank from overwriting states
+// a slow one is still merging, and a slot still holding call e - 2's words never passes for call
+// e's. The epoch lives in device memory, so a captured CUDA graph replays correctly.
 static __device__ unsigned int g_peer_fault = 0u;
 constexpr int kMaxPeers = 8;
 constexpr int64_t kPeerHeaderBytes = 256;
@@ -279,10 +281,8 @@ constexpr long long kPeerWaitCycles = 1ll << 31;
 constexpr unsigned int kPeerMagic = 0x4e425045u;  // "NBPE": written by peer_init_kernel
 struct PeerHeader {
     unsigned int ep;          // epoch of the last completed exchange on this rank
-    unsigned int arrive;      // CTAs of the fused fold + push that have stored their states
-    unsigned int merge_done;  // the same for the merge
-    unsigned int pad;
-    unsigned int flag[kMaxPeers];
+    unsigned int merge_done;  // CTAs of the merge that have finished reading the slots
+    unsigned int pad[2 + kMaxPeers];
     // The layout this buffer was sized and initialised for (nb200_peer_init). Every push checks the
     // destination's layout and every merge its own before touching the slots: a call whose
     // (rows, world, nparts) differ, or a buffer never initialised, stores nothing.
@@ -310,27 +310,52 @@ __device__ __forceinline__ bool peer_layout_ok(const unsigned char* buf, int64_t
     return h->magic == kPeerMagic && h->rows == rows && h->nparts == nparts && h->world == world;
 }
 
-// Records the layout in a buffer's header and clears its epoch, counters and flags (one thread).
+// A tagged slot: state v (m, acc, seen, status as in the float4 state layout) of call e.
+__device__ __forceinline__ void peer_slot_store(void* slot, const float4& v, unsigned int e) {
+    const unsigned int tag = (e << 5) | ((unsigned int)(__float_as_int(v.w) & 15) << 1) |
+                             (unsigned int)(__float_as_int(v.z) & 1);
+    const unsigned long long a = (unsigned long long)__float_as_uint(v.x) | ((unsigned long long)e << 32);
+    const unsigned long long b = (unsigned long long)__float_as_uint(v.y) | ((unsigned long long)tag << 32);
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(slot), "l"(a), "l"(b) : "memory");
+}
+// The two words of a tagged slot, and whether they carry epoch e (then v holds the state).
+__device__ __forceinline__ void peer_slot_raw(const void* slot, unsigned long long& a, unsigned long long& b) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(slot) : "memory");
+}
+__device__ __forceinline__ bool peer_slot_ready(unsigned long long a, unsigned long long b, unsigned int e, float4& v) {
+    const unsigned int tag = (unsigned int)(b >> 32);
+    if ((unsigned int)(a >> 32) != e || (tag >> 5) != (e & 0x07ffffffu)) return false;
+    v = make_float4(__uint_as_float((unsigned int)a), __uint_as_float((unsigned int)b), __int_as_float((int)(tag & 1u)),
+                    __int_as_float((int)((tag >> 1) & 15u)));
+    return true;
+}
+
+// Records the layout in a buffer's header, clears its epoch and counter (CTA 0, thread 0) and
+// zeroes every slot (no slot then carries an epoch of a call to come).
 __global__ void peer_init_kernel(unsigned char* buf, int64_t rows, int64_t nparts, int world) {
     pdl_wait();
     pdl_trigger();
-    PeerHeader* h = reinterpret_cast<PeerHeader*>(buf);
-    h->ep = 0u;
-    h->arrive = 0u;
-    h->merge_done = 0u;
-    h->pad = 0u;
-    for (int r = 0; r < kMaxPeers; ++r) h->flag[r] = 0u;
-    h->rows = rows;
-    h->nparts = nparts;
-    h->world = world;
-    __threadfence_system();
-    h->magic = kPeerMagic;
-    __threadfence_system();
+    const int64_t nslots = 2 * rows * world * nparts;
+    uint4* slots = reinterpret_cast<uint4*>(buf + kPeerHeaderBytes);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nslots; i += (int64_t)gridDim.x * blockDim.x)
+        slots[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        PeerHeader* h = reinterpret_cast<PeerHeader*>(buf);
+        h->ep = 0u;
+        h->merge_done = 0u;
+        for (int r = 0; r < 2 + kMaxPeers; ++r) h->pad[r] = 0u;
+        h->rows = rows;
+        h->nparts = nparts;
+        h->world = world;
+        __threadfence_system();
+        h->magic = kPeerMagic;
+        __threadfence_system();
+    }
 }
 
-// One CTA per destination rank: CTA r checks rank r's recorded layout, writes this rank's states
-// into rank r's buffer, fences at system scope and raises flag[rank] there, so each flag follows
-// exactly the stores it announces. A destination whose layout differs gets nothing (fault bit 3).
+// One CTA per destination rank: CTA r checks rank r's recorded layout and writes this rank's
+// states, tagged with the call's epoch, into rank r's buffer. A destination whose layout differs
+// gets nothing (fault bit 3).
 constexpr int kPushThreads = 512;
 __global__ void __launch_bounds__(kPushThreads)
 peer_push_kernel(const nb200_state* __restrict__ states, int64_t rows, int64_t nlocal, int64_t nparts,
@@ -354,16 +379,54 @@ peer_push_kernel(const nb200_state* __restrict__ states, int64_t rows, int64_t n
         // parts past this rank's own count are empty states (unequal shard widths)
         const float4 v = part < nlocal ? reinterpret_cast<const float4*>(states)[row * nlocal + part]
                                        : make_float4(-NB200_INF, 0.f, 0.f, 0.f);
-        slots[((par * rows + row) * world + rank) * nparts + part] = v;
+        peer_slot_store(&slots[((par * rows + row) * world + rank) * nparts + part], v, e);
     }
-    // One system-scope fence by the flagging thread: the barrier orders every thread's stores
-    // before it and the fence is cumulative, so they are visible before the flag is.
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        unsigned int* f = &reinterpret_cast<PeerHeader*>(dst)->flag[rank];
-        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
+}
+
+// One warp per row, as merge_row: lane l reads the contiguous run of states [l*k, (l+1)*k) of the
+// row's world * nparts, eight slots at a time (all eight loads issued before any is tested), each
+// until it carries epoch e -- bounded: about a second of SM cycles, then the row is left unwritten
+// and the caller sets fault bit 2 -- merges its run left to right, then the 32 runs combine in
+// merge_row's tree.
+template <int S>
+__device__ __forceinline__ bool peer_merge_row(const float4* row, int64_t total, unsigned int e, int lane,
+                                               const Params& p, St& out, long long t0) {
+    constexpr int kBatch = 8;
+    const int64_t k = (total + 31) / 32;
+    const int64_t lo = (int64_t)lane * k, hi = min(lo + k, total);
+    St s = empty_state();
+    bool ok = true;
+    for (int64_t j0 = lo; j0 < hi && ok; j0 += kBatch) {
+        float4 v[kBatch];
+        unsigned int pending = 0u;  // bit u: slot j0 + u not yet carrying epoch e
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+            if (j0 + u < hi) pending |= 1u << u;
+        for (unsigned int it = 0; pending; ++it) {
+            unsigned long long a[kBatch], b[kBatch];
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u)
+                if ((pending >> u) & 1u) peer_slot_raw(row + j0 + u, a[u], b[u]);
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u)
+                if (((pending >> u) & 1u) && peer_slot_ready(a[u], b[u], e, v[u])) pending &= ~(1u << u);
+            if (pending && (it & 63u) == 63u && clock64() - t0 > kPeerWaitCycles) {
+                ok = false;
+                break;
+            }
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int u = 0; u < kBatch; ++u)
+            if (j0 + u < hi) s = merge<S>(s, St{v[u].x, v[u].y, __float_as_int(v[u].z), __float_as_int(v[u].w)}, p);
     }
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const St other = shfl_state(s, o);
+        s = (lane & o) ? merge<S>(other, s, p) : merge<S>(s, other, p);
+    }
+    out = s;
+    return __all_sync(0xffffffffu, ok);
 }
 
 template <int S, typename T>
@@ -377,32 +440,18 @@ peer_merge_kernel(unsigned char* own, T* __restrict__ out, int64_t rows, int64_t
         return;
     }
     const unsigned int e = *reinterpret_cast<volatile unsigned int*>(&h->ep) + 1u;
-    // Thread r waits for rank r's flag, so the ranks' system-scope polls overlap.
-    bool ok = true;
-    if (threadIdx.x < world) {
-        const long long t0 = clock64();
-        for (unsigned int it = 0;; ++it) {
-            unsigned int f;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(&h->flag[threadIdx.x]) : "memory");
-            if ((int)(f - e) >= 0) break;
-            if ((it & 63u) == 63u && clock64() - t0 > kPeerWaitCycles) {
-                ok = false;
-                atomicOr(&g_peer_fault, 4u);
-                break;
-            }
-        }
-    }
-    const bool arrived = __syncthreads_and(ok) != 0;
-    if (arrived) {
-        const int lane = threadIdx.x & 31;
-        const int64_t total = (int64_t)world * nparts;
-        const nb200_state* slots =
-            reinterpret_cast<const nb200_state*>(own + kPeerHeaderBytes) + (int64_t)(e & 1u) * rows * total;
-        const int64_t gid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-        const int64_t ng = (int64_t)gridDim.x * (blockDim.x >> 5);
-        for (int64_t r = gid; r < rows; r += ng) {
-            const St s = merge_row<S, true>(slots + r * total, total, 1, lane, p);
+    const int lane = threadIdx.x & 31;
+    const int64_t total = (int64_t)world * nparts;
+    const float4* slots = reinterpret_cast<const float4*>(own + kPeerHeaderBytes) + (int64_t)(e & 1u) * rows * total;
+    const int64_t gid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t ng = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const long long t0 = clock64();
+    for (int64_t r = gid; r < rows; r += ng) {
+        St s;
+        if (peer_merge_row<S>(slots + r * total, total, e, lane, p, s, t0)) {
             if (lane == 0) out[r] = Elem<T>::from_f(finalize<S>(s, p));
+        } else if (lane == 0) {
+            atomicOr(&g_peer_fault, 4u);
         }
     }
     __syncthreads();
@@ -412,15 +461,12 @@ peer_merge_kernel(unsigned char* own, T* __restrict__ out, int64_t rows, int64_t
     }
 }
 
-// Two launches per call of the column-sharded split (nb200_peer_fold): the partial fold and the
-// push in one kernel, then peer_merge_kernel above.
-//   1. Each warp folds span items of this rank's shard (the split plan's span fold, so the states
-//      are bit-identical to nb200_fold_partial's) and lanes 0..world-1 store the item's state into
-//      slot `rank` of every rank's buffer (parts past this rank's chunk count are stored empty).
-//   2. Each CTA fences at system scope and counts itself in; the last CTA raises flag[rank] = e in
-//      every rank's buffer after another system-scope fence.
-// No CTA waits here: the merge kernel, launched behind it, waits for the flags. Layouts are checked
-// before any store (fault bit 3: nothing stored, no flag raised).
+// Two launches per call of the column-sharded split (nb200_peer_fold): the partial fold storing
+// its states straight into every rank's buffer, then peer_merge_kernel above. Each warp folds span
+// items of this rank's shard (the split plan's span fold, so the states are bit-identical to
+// nb200_fold_partial's) and lanes 0..world-1 store the item's tagged state into slot `rank` of
+// every rank's buffer (parts past this rank's chunk count are stored empty). Nothing waits here;
+// layouts are checked before any store (fault bit 3: nothing stored).
 template <int S, typename T>
 __global__ void __launch_bounds__(kLdgThreads, 6)
 peer_span_kernel(const T* __restrict__ x, LdgSpan pl, int64_t slot_parts, Params p, PeerPtrs peers, int world,
@@ -453,24 +499,7 @@ peer_span_kernel(const T* __restrict__ x, LdgSpan pl, int64_t slot_parts, Params
             const St w = span_item_state<S, T>(x, pl, row * pl.nparts + part, lane, p);
             v = make_float4(w.m, w.acc, __int_as_float(w.seen), __int_as_float(w.status));
         }
-        if (mine) mine[((par * rows + row) * world + rank) * slot_parts + part] = v;
-    }
-    // The CTA's stores reach the count through thread 0: the barrier orders them before its
-    // (cumulative) system-scope fence, the fence before its increment; the last CTA fences again
-    // after seeing every increment and then raises the flags.
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        if (atomicAdd(&h->arrive, 1u) == gridDim.x - 1) {
-            atomicExch(&h->arrive, 0u);
-            __threadfence_system();
-#pragma unroll
-            for (int r = 0; r < kMaxPeers; ++r) {
-                if (r >= world) break;
-                unsigned int* f = &reinterpret_cast<PeerHeader*>(peers.p[r])->flag[rank];
-                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
-            }
-        }
+        if (mine) peer_slot_store(&mine[((par * rows + row) * world + rank) * slot_parts + part], v, e);
     }
 }
 
@@ -835,7 +864,9 @@ int64_t peer_buffer_bytes(int64_t rows, int64_t world, int64_t nparts) {
 int peer_max_world() { return kMaxPeers; }
 
 int launch_peer_init(void* buffer, int64_t rows, int64_t nparts, int world, cudaStream_t st) {
-    launch_pdl(peer_init_kernel, 1, 1, 0, st, static_cast<unsigned char*>(buffer), rows, nparts, world);
+    const int64_t nslots = 2 * rows * world * nparts;
+    const int g = (int)std::min<int64_t>(std::max<int64_t>((nslots + 255) / 256, 1), 1024);
+    launch_pdl(peer_init_kernel, g, 256, 0, st, static_cast<unsigned char*>(buffer), rows, nparts, world);
     count_launch();
     return finish_launch("nb200_peer_init");
 }

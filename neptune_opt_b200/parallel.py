@@ -13,8 +13,9 @@ The one exchange is the split plan for ultra-wide rows when the reduction axis i
 across GPUs (`sharded_split_fold`): each rank folds its column shard into per-row chunk states
 (16 bytes each) and every rank merges all of them in ascending (rank, chunk) order -- the same
 certified order as the single-GPU split plan. The states move either through one all-gather or,
-with a `PeerExchange`, through NVLink peer memory: the pushing kernel stores them into every rank's
-buffer and raises a flag, the merging kernel waits for all flags (no collective, no host step).
+with a `PeerExchange`, through NVLink peer memory: the folding (or pushing) kernel stores them into
+every rank's buffer, each state tagged with the call's epoch inside its 16 bytes, and the merging
+kernel reads each state until it carries that epoch (no collective, no flag, no host step).
 """
 from __future__ import annotations
 
@@ -130,12 +131,12 @@ class PeerExchange:
     Every rank allocates one buffer of `nb200_peer_buffer_bytes(rows, world, nparts)` bytes on its
     GPU, records the layout in it (`nb200_peer_init`) and maps the others' with CUDA IPC (handles
     swapped once with all_gather_object). A `sharded_split_fold(..., exchange=ex)` call then moves
-    the chunk states with two kernels -- stores into every peer's buffer plus a flag, and a merge
-    that waits for all flags -- instead of a collective. `nparts` is the per-rank slot width: the
+    the chunk states with two kernels -- epoch-tagged stores into every peer's buffer, and a merge
+    that reads each state until it carries the call's epoch -- instead of a collective. `nparts` is the per-rank slot width: the
     largest number of chunks any rank's shard has. Create it on every rank of the group (it
     synchronises them) and `close()` it on every rank.
 
-    Faults: the merge's wait for the ranks' flags is bounded (about a second); when it runs out
+    Faults: the merge's wait for the ranks' states is bounded (about a second); when it runs out
     (a rank did not push) the kernel sets bit 2 of `nb200_stream_fault` and leaves the output
     unwritten, and a call whose layout differs from a buffer's sets bit 3 and stores nothing.
     Nothing on the host notices by itself: pass `check=True` to `sharded_split_fold` (it
@@ -251,7 +252,7 @@ class PeerExchange:
     def fold(self, name, params, x_shard, ncols_total, chunk, out):
         """The whole call in two launches (nb200_peer_fold): fold this rank's contiguous shard
         x_shard [rows, width] in `chunk`-column chunks storing the states straight into every rank's
-        buffer (its last CTA raises the flags), then wait for everyone's and merge into out[rows].
+        buffer, tagged with the call's epoch), then wait for everyone's and merge into out[rows].
         Same result, bit for bit, as the partial fold followed by `exchange_and_merge`."""
         from neptune_opt_b200 import _lib
         from neptune_opt_b200.skeletons import SKELETONS, checked_params
@@ -369,7 +370,7 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
             if bits & 0xC:
                 exchange.faulted = True
                 raise RuntimeError(f"peer exchange fault (bits {bits:#x}): "
-                                   + ("a rank's flag never arrived; " if bits & 4 else "")
+                                   + ("a rank's states never arrived; " if bits & 4 else "")
                                    + ("a buffer's layout differs from the call's; " if bits & 8 else "")
                                    + "close the exchange on every rank and set up a new one")
         return out

@@ -1,8 +1,8 @@
 """Two-GPU run of the column-sharded split plan (the one multi-GPU path with an exchange).
 
 Each rank folds its column shard of a bf16 [64, 100000] block into chunk states; they move either
-through one NCCL all-gather or through NVLink peer memory (PeerExchange: stores into every rank's
-buffer, a flag per rank, a merge that waits for all flags -- the fold storing into the buffers
+through one NCCL all-gather or through NVLink peer memory (PeerExchange: epoch-tagged stores into
+every rank's buffer, a merge that reads each state until it carries the call's epoch -- the fold storing into the buffers
 itself, or a partial fold plus push and merge kernels, alternating call by call), and every rank merges them in
 ascending (rank, chunk) order. Both must equal, bit for bit, the single-GPU merge of the same states in the
 same order, match the oracle within 1 bf16 ulp, agree with each other on inputs that change from

@@ -4,7 +4,7 @@ Two exchange buffers on the same device stand in for two ranks' buffers, so the 
 checks run without a second GPU:
 * world = 1: push + merge, and the fused nb200_peer_fold (fold storing into the buffers, then the
   merge), equal nb200_fold_merge of the same states, bit for bit, call after call (mixing forms);
-* a rank that never pushes: the merge's bounded wait for its flag runs out after about a second,
+* a rank that never pushes: the merge's bounded wait for its states runs out after about a second,
   fault bit 2 (0x4) is reported once, and the NaN-filled output is left unwritten -- after the push
   kernel and after the fused form;
 * a buffer initialised for another layout: the push stores nothing into it and the merge reads
@@ -133,7 +133,7 @@ def test_merge_wait_runs_out_when_a_rank_never_pushes():
     L.check(_push(lib, states, ROWS, nparts, [buf0, buf1], 0, buf0), "push")  # "rank 1" never pushes
     L.check(_merge(lib, L, buf0, ROWS, nparts, 2, out), "peer merge")
     torch.cuda.synchronize()
-    assert L.stream_fault() & 0x4, "the merge's wait for the missing rank's flag did not report running out"
+    assert L.stream_fault() & 0x4, "the merge's wait for the missing rank's states did not report running out"
     assert torch.isnan(out).all(), "the merge wrote an output although a rank's states never arrived"
     assert L.stream_fault() == 0, "the fault word was not cleared by reading it"
     # the fused form: its merge's wait for "rank 1" runs out the same way
