@@ -106,7 +106,7 @@ uint64_t nb200_launch_count(void);
 /* Reads and clears the fault bits of the kernels with device-side waits or checks (bit 0: a
  * bounded wait on a bulk copy in a streaming kernel ran out and the kernel stopped early; bit 1: a
  * bounded wait in the attention kernel ran out and its output was left unwritten; bit 2: the peer
- * merge's bounded wait for the ranks' states ran out, output unwritten; bit 3: a peer push or merge
+ * merge's bounded wait for the ranks' states ran out, those rows written as NaN; bit 3: a peer push or merge
  * found a buffer whose recorded layout differs from the call's, nothing stored or read).
  * Synchronous. No counterpart in the reference, whose Triton kernels have no device-side waits. */
 int nb200_stream_fault(uint32_t* bits);
@@ -195,7 +195,7 @@ int nb200_fold_merge(int skeleton, const nb200_params* params,
  *                          peers[rank] = buffer), each state tagged with the call's epoch inside
  *                          its 16 bytes (no fence, no flag);
  *   nb200_peer_merge    -> reads each state until it carries the call's epoch (bounded: about a
- *                          second, then bit 2 of nb200_stream_fault and the row is left unwritten), merges
+ *                          second, then bit 2 of nb200_stream_fault and the row reads NaN), merges
  *                          each row's world * nparts states in ascending (rank, part) order into
  *                          out[rows] -- the result of nb200_fold_merge on the gathered states.
  * Every rank makes the same calls in the same order with the same rows and nparts; a call's epoch
@@ -203,7 +203,7 @@ int nb200_fold_merge(int skeleton, const nb200_params* params,
  * Layout checks: before storing into a destination, the push kernel compares the call's
  * (rows, world, nparts) with the layout recorded in this rank's and the destination's header; the
  * merge compares its own. On a mismatch (or a buffer never initialised) nothing is stored or read,
- * bit 3 of nb200_stream_fault is set and the output is left unwritten. After fault bit 2 or 3 the
+ * bit 3 of nb200_stream_fault is set and the merge writes every row as NaN. After fault bit 2 or 3 the
  * ranks' epochs no longer agree: close the exchange on every rank and set it up again. */
 int64_t nb200_peer_buffer_bytes(int64_t rows, int64_t world, int64_t nparts);
 int nb200_peer_init(void* buffer, int64_t rows, int world, int64_t nparts, void* stream);

@@ -270,7 +270,7 @@ merge_kernel(const nb200_state* __restrict__ states, T* __restrict__ out, int64_
 // rank's buffer (stores over NVLink, no fence, no flag); peer_merge_kernel reads each state until
 // both its words carry epoch e (bounded), merges each row's world * nparts states in ascending
 // (rank, part) order -- the order of the single-GPU split plan -- and its last CTA records e as
-// completed. A rank can be at most one call ahead of another (its next stores follow its own
+// completed. Rows it cannot produce (a state that never arrived, a layout that differs) read NaN. A rank can be at most one call ahead of another (its next stores follow its own
 // merge, which needs everyone's states), so two parities keep a fast rank from overwriting states
 // a slow one is still merging, and a slot still holding call e - 2's words never passes for call
 // e's. The epoch lives in device memory, so a captured CUDA graph replays correctly.
@@ -385,8 +385,8 @@ peer_push_kernel(const nb200_state* __restrict__ states, int64_t rows, int64_t n
 
 // One warp per row, as merge_row: lane l reads the contiguous run of states [l*k, (l+1)*k) of the
 // row's world * nparts, eight slots at a time (all eight loads issued before any is tested), each
-// until it carries epoch e -- bounded: about a second of SM cycles, then the row is left unwritten
-// and the caller sets fault bit 2 -- merges its run left to right, then the 32 runs combine in
+// until it carries epoch e -- bounded: about a second of SM cycles, then the caller writes the row
+// as NaN and sets fault bit 2 -- merges its run left to right, then the 32 runs combine in
 // merge_row's tree.
 template <int S>
 __device__ __forceinline__ bool peer_merge_row(const float4* row, int64_t total, unsigned int e, int lane,
@@ -435,8 +435,10 @@ peer_merge_kernel(unsigned char* own, T* __restrict__ out, int64_t rows, int64_t
     pdl_wait();
     pdl_trigger();
     PeerHeader* h = reinterpret_cast<PeerHeader*>(own);
-    if (!peer_layout_ok(own, rows, nparts, world)) {  // nothing read, nothing written, epoch kept
-        if (threadIdx.x == 0) atomicOr(&g_peer_fault, 8u);
+    if (!peer_layout_ok(own, rows, nparts, world)) {  // nothing read, every row NaN, epoch kept
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(&g_peer_fault, 8u);
+        for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += (int64_t)gridDim.x * blockDim.x)
+            out[r] = Elem<T>::from_f(NB200_NAN);
         return;
     }
     const unsigned int e = *reinterpret_cast<volatile unsigned int*>(&h->ep) + 1u;
@@ -450,8 +452,9 @@ peer_merge_kernel(unsigned char* own, T* __restrict__ out, int64_t rows, int64_t
         St s;
         if (peer_merge_row<S>(slots + r * total, total, e, lane, p, s, t0)) {
             if (lane == 0) out[r] = Elem<T>::from_f(finalize<S>(s, p));
-        } else if (lane == 0) {
+        } else if (lane == 0) {  // a state never arrived: the row reads NaN
             atomicOr(&g_peer_fault, 4u);
+            out[r] = Elem<T>::from_f(NB200_NAN);
         }
     }
     __syncthreads();
@@ -468,7 +471,7 @@ peer_merge_kernel(unsigned char* own, T* __restrict__ out, int64_t rows, int64_t
 // every rank's buffer (parts past this rank's chunk count are stored empty). Nothing waits here;
 // layouts are checked before any store (fault bit 3: nothing stored).
 template <int S, typename T>
-__global__ void __launch_bounds__(kLdgThreads, 6)
+__global__ void __launch_bounds__(kLdgThreads, 7)
 peer_span_kernel(const T* __restrict__ x, LdgSpan pl, int64_t slot_parts, Params p, PeerPtrs peers, int world,
                  int rank, unsigned char* own) {
     pdl_wait();

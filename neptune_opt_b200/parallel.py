@@ -137,8 +137,9 @@ class PeerExchange:
     synchronises them) and `close()` it on every rank.
 
     Faults: the merge's wait for the ranks' states is bounded (about a second); when it runs out
-    (a rank did not push) the kernel sets bit 2 of `nb200_stream_fault` and leaves the output
-    unwritten, and a call whose layout differs from a buffer's sets bit 3 and stores nothing.
+    (a rank did not push) the kernel sets bit 2 of `nb200_stream_fault` and writes those rows as
+    NaN, and a call whose layout differs from a buffer's sets bit 3 and stores nothing (a merge on
+    such a buffer writes every row as NaN).
     Nothing on the host notices by itself: pass `check=True` to `sharded_split_fold` (it
     synchronises and raises), or read `neptune_opt_b200._lib.stream_fault()`. After either fault
     the ranks' epochs disagree, so this exchange refuses further calls: close it on every rank and
@@ -324,8 +325,8 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
     largest rank's chunk count) the states move through NVLink peer memory instead of an
     all-gather; the result is the same bit for bit -- in two launches (`PeerExchange.fold`: the fold
     stores into the peers' buffers itself) when the shard is contiguous and aligned and `fused` is
-    set, else as a partial fold plus the exchange's push and merge kernels. The exchange's output starts as NaN, so a merge
-    whose bounded wait ran out leaves NaN rather than stale memory; `check=True` synchronises after
+    set, else as a partial fold plus the exchange's push and merge kernels. A merge whose bounded
+    wait ran out writes its rows as NaN rather than leaving stale memory; `check=True` synchronises after
     the merge and raises if a wait ran out or a layout differed (marking the exchange unusable).
     """
     import torch
@@ -357,7 +358,7 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
         if exchange.nparts != max_parts or exchange.world != world:
             raise ValueError(f"the exchange holds {exchange.nparts} parts per rank for {exchange.world} ranks; "
                              f"this layout needs {max_parts} for {world}")
-        out = torch.full((rows,), float("nan"), dtype=x_shard.dtype, device=x_shard.device)
+        out = torch.empty(rows, dtype=x_shard.dtype, device=x_shard.device)  # rows the merge cannot produce read NaN
         if fused and partial_fn is _cuda_partial and exchange.fold_eligible(x_shard, chunk):
             exchange.fold(name, params, x_shard, ncols_total, chunk, out)
         else:

@@ -5,7 +5,7 @@ checks run without a second GPU:
 * world = 1: push + merge, and the fused nb200_peer_fold (fold storing into the buffers, then the
   merge), equal nb200_fold_merge of the same states, bit for bit, call after call (mixing forms);
 * a rank that never pushes: the merge's bounded wait for its states runs out after about a second,
-  fault bit 2 (0x4) is reported once, and the NaN-filled output is left unwritten -- after the push
+  fault bit 2 (0x4) is reported once, and the merge writes the rows as NaN -- after the push
   kernel and after the fused form;
 * a buffer initialised for another layout: the push stores nothing into it and the merge reads
   nothing from it (fault bit 3, 0x8).
@@ -129,17 +129,17 @@ def test_merge_wait_runs_out_when_a_rank_never_pushes():
     keep1, buf1 = _buffer(lib, ROWS, 2, nparts)
     for b in (buf0, buf1):
         _init(lib, L, b, ROWS, 2, nparts)
-    out = torch.full((ROWS,), float("nan"), device="cuda")
+    out = torch.zeros(ROWS, device="cuda")  # the merge writes NaN rows
     L.check(_push(lib, states, ROWS, nparts, [buf0, buf1], 0, buf0), "push")  # "rank 1" never pushes
     L.check(_merge(lib, L, buf0, ROWS, nparts, 2, out), "peer merge")
     torch.cuda.synchronize()
     assert L.stream_fault() & 0x4, "the merge's wait for the missing rank's states did not report running out"
-    assert torch.isnan(out).all(), "the merge wrote an output although a rank's states never arrived"
+    assert torch.isnan(out).all(), "the merge did not write NaN rows although a rank's states never arrived"
     assert L.stream_fault() == 0, "the fault word was not cleared by reading it"
     # the fused form: its merge's wait for "rank 1" runs out the same way
     for b in (buf0, buf1):
         _init(lib, L, b, ROWS, 2, nparts)
-    out = torch.full((ROWS,), float("nan"), device="cuda")
+    out = torch.zeros(ROWS, device="cuda")  # the merge writes NaN rows
     L.check(_fold(lib, L, x, nparts, [buf0, buf1], 0, buf0, out), "peer fold")
     torch.cuda.synchronize()
     assert L.stream_fault() & 0x4, "the fused form's wait did not report running out"
@@ -170,7 +170,7 @@ def test_layout_mismatch_stores_and_reads_nothing():
     torch.cuda.synchronize()
     assert L.stream_fault() & 0x8, "the push did not report the destination's layout mismatch"
     assert torch.equal(buf1, before), "the push stored into a buffer of another layout"
-    out = torch.full((ROWS,), float("nan"), device="cuda")
+    out = torch.zeros(ROWS, device="cuda")  # the merge writes NaN rows
     L.check(_merge(lib, L, buf1, ROWS, nparts, 2, out), "peer merge")
     torch.cuda.synchronize()
     assert L.stream_fault() & 0x8 and torch.isnan(out).all()
