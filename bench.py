@@ -57,7 +57,8 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--region", default=None,
                     help="time one region only (rms_norm, softmax_lse, logsumexp, l2_normalize, "
-                         "wide_logsumexp_split, segment_sum, segment_mean, attention, attention_causal, "
+                         "wide_logsumexp_split, wide_logsumexp_split_1024, segment_sum, segment_mean, attention, "
+                         "attention_causal, "
                          "lse_1x262144, rms_1x65536, lse_256x16384) "
                          "and print its line; "
                          "used for ncu captures of a single kernel")
@@ -280,8 +281,10 @@ def make_l2(torch, NB, seed):
             "launches": 1, "buffers": nbuf, "io0": {"x": xs[0], "y": ys[0], "norm": norm}, "desc": f"L2-normalize fp16 x[{rows},{ncols}] -> y, norm"}
 
 
-def make_wide_lse(torch, NB, seed):
-    rows, ncols, block = 512, 262144, 16384
+def make_wide_lse(torch, NB, seed, block=16384):
+    """BASELINE config 3b: the split plan in 16384-column chunks; block=1024 is the reference's
+    default split BLOCK (what its front end emits), on the same input."""
+    rows, ncols = 512, 262144
     g = torch.Generator(device="cuda").manual_seed(seed)
     nbuf = 2
     xs = [(torch.randn(rows, ncols, device="cuda", generator=g) * 3.0).to(torch.bfloat16) for _ in range(nbuf)]
@@ -290,7 +293,8 @@ def make_wide_lse(torch, NB, seed):
     def step(i):
         NB.template.launch_reduction("logsumexp", "split", xs[i % nbuf], out, rows, ncols, block, 8, {"tiny": 0.0})
 
-    return {"name": "wide_logsumexp_split", "step": step, "bytes": rows * ncols * 2 + rows * 2, "rows": rows,
+    return {"name": "wide_logsumexp_split" + ("" if block == 16384 else f"_{block}"), "step": step,
+            "bytes": rows * ncols * 2 + rows * 2, "rows": rows,
             "launches": 2, "buffers": nbuf, "io0": {"x": xs[0], "out": out},
             "desc": f"logsumexp bf16 x[{rows},{ncols}] N(0,3^2), split plan {block}-column chunks -> [{rows}]"}
 
@@ -733,6 +737,7 @@ def run_reference(args):
 REGION_MAKERS = {
     "rms_norm": make_rms, "softmax_lse": make_softmax, "logsumexp": make_lse, "l2_normalize": make_l2,
     "wide_logsumexp_split": make_wide_lse,
+    "wide_logsumexp_split_1024": lambda t, nb, s: make_wide_lse(t, nb, s, block=1024),
     "segment_sum": lambda t, nb, s: make_segments(t, nb, s, "sum"),
     "segment_mean": lambda t, nb, s: make_segments(t, nb, s, "mean"),
     "attention": make_attention,
@@ -841,6 +846,7 @@ def main():
     regions = {}
     if not args.no_regions:
         makers = [make_softmax, make_lse, make_l2, make_wide_lse,
+                  lambda t, nb, s: make_wide_lse(t, nb, s, block=1024),
                   lambda t, nb, s: make_segments(t, nb, s, "sum"), lambda t, nb, s: make_segments(t, nb, s, "mean")]
         for maker in makers:
             r = maker(torch, NB, 2000 + dist.rank)
