@@ -309,7 +309,7 @@ class PeerExchange:
 
 def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: int = 16384, group=None,
                        partial_fn=None, merge_fn=None, widths=None, exchange=None, check: bool = False,
-                       fused: bool = True):
+                       fused: bool | None = None):
     """Fold rows whose columns are sharded across the ranks of `group`, rank order = column order.
 
     Each rank passes its own [rows, width_r] block (the ranks' blocks concatenated along columns in
@@ -325,7 +325,10 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
     largest rank's chunk count) the states move through NVLink peer memory instead of an
     all-gather; the result is the same bit for bit -- in two launches (`PeerExchange.fold`: the fold
     stores into the peers' buffers itself) when the shard is contiguous and aligned and `fused` is
-    set, else as a partial fold plus the exchange's push and merge kernels. A merge whose bounded
+    set, else as a partial fold plus the exchange's push and merge kernels. `fused=None` picks by
+    the group size as measured on B200 (bf16 [512, 262144], 16384-column chunks): the two-launch
+    form at 2 ranks (43.6 vs 46.1 µs per call), the three-launch form at 8 (29.2 vs 41.0 µs), where
+    every rank's fold storing into seven peers' buffers costs more than one push kernel. A merge whose bounded
     wait ran out writes its rows as NaN rather than leaving stale memory; `check=True` synchronises after
     the merge and raises if a wait ran out or a layout differed (marking the exchange unusable).
     """
@@ -359,6 +362,8 @@ def sharded_split_fold(name, x_shard, ncols_total: int, *, params=None, chunk: i
             raise ValueError(f"the exchange holds {exchange.nparts} parts per rank for {exchange.world} ranks; "
                              f"this layout needs {max_parts} for {world}")
         out = torch.empty(rows, dtype=x_shard.dtype, device=x_shard.device)  # rows the merge cannot produce read NaN
+        if fused is None:
+            fused = world <= 2
         if fused and partial_fn is _cuda_partial and exchange.fold_eligible(x_shard, chunk):
             exchange.fold(name, params, x_shard, ncols_total, chunk, out)
         else:

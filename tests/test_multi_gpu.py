@@ -1,4 +1,5 @@
-"""Two-GPU run of the column-sharded split plan (the one multi-GPU path with an exchange).
+"""Multi-GPU run of the column-sharded split plan (the one multi-GPU path with an exchange), on
+every GPU of the box up to 8.
 
 Each rank folds its column shard of a bf16 [64, 100000] block into chunk states; they move either
 through one NCCL all-gather or through NVLink peer memory (PeerExchange: epoch-tagged stores into
@@ -6,8 +7,8 @@ every rank's buffer, a merge that reads each state until it carries the call's e
 itself, or a partial fold plus push and merge kernels, alternating call by call), and every rank merges them in
 ascending (rank, chunk) order. Both must equal, bit for bit, the single-GPU merge of the same states in the
 same order, match the oracle within 1 bf16 ulp, agree with each other on inputs that change from
-call to call, and replay from a captured CUDA graph. Runs as two spawned processes; skipped with
-fewer than two GPUs.
+call to call, and replay from a captured CUDA graph. Runs as one spawned process per GPU; skipped
+with fewer than two GPUs.
 """
 from __future__ import annotations
 
@@ -99,10 +100,11 @@ def test_sharded_split_over_nccl_matches_single_gpu(tmp_path, oracle_mod):
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
+    world = min(torch.cuda.device_count(), 8)  # every GPU of the box, up to the exchange's 8 ranks
     result = str(tmp_path / "r0.pt")
     ctx = mp.get_context("spawn")
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, result)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, result)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -119,8 +121,8 @@ def test_sharded_split_over_nccl_matches_single_gpu(tmp_path, oracle_mod):
     gen = torch.Generator().manual_seed(21)
     x = (torch.randn(ROWS, NCOLS, generator=gen) * 3).to(torch.bfloat16)
     states = []
-    for r in range(2):  # the same shards and chunking on one GPU, states in (rank, chunk) order
-        c0, c1 = shard_rows(NCOLS, 2, r)
+    for r in range(world):  # the same shards and chunking on one GPU, states in (rank, chunk) order
+        c0, c1 = shard_rows(NCOLS, world, r)
         states.append(_cuda_partial("logsumexp", {"tiny": 0.0}, x[:, c0:c1].contiguous().cuda(), c0, NCOLS, CHUNK))
     width = max(s.shape[1] for s in states)
     for i, s in enumerate(states):
