@@ -213,7 +213,8 @@ int nb200_peer_merge(int skeleton, const nb200_params* params, void* buffer, int
                      int64_t nparts, int world, void* out, int dtype, void* stream);
 /* The same call in TWO launches (no counterpart in the reference): the partial fold of this rank's
  * column shard x[rows, ncols_shard] (contiguous rows, 16-byte aligned, row stride, width and
- * chunk_cols multiples of 16 bytes) storing its tagged chunk states straight into every rank's
+ * chunk_cols multiples of 16 bytes, chunks wider than 4 KB -- narrower ones return
+ * NB200_ERR_UNSUPPORTED: use the push form) storing its tagged chunk states straight into every rank's
  * buffer (nb200_fold_partial + nb200_peer_push in one kernel), then the
  * merge of nb200_peer_merge. ncols_total (all ranks' columns) sets the skeletons' 1/N as in
  * nb200_fold_partial. Same buffers, layout checks, fault bits, epochs, parities and protocol as

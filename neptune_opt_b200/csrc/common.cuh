@@ -127,6 +127,12 @@ template <> struct Elem<__half> {
     }
 };
 
+// [v0, v1): part i of n items cut into k contiguous, nearly equal parts.
+__device__ __forceinline__ void split_range(int64_t n, int64_t k, int64_t i, int64_t& v0, int64_t& v1) {
+    v0 = n * i / k;
+    v1 = n * (i + 1) / k;
+}
+
 // Streaming 16-byte load/store: data read once should not displace reused lines.
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
     return __ldcs(reinterpret_cast<const uint4*>(p));

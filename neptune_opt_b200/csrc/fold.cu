@@ -470,7 +470,7 @@ peer_merge_kernel(unsigned char* own, T* __restrict__ out, int64_t rows, int64_t
 // nb200_fold_partial's) and lanes 0..world-1 store the item's tagged state into slot `rank` of
 // every rank's buffer (parts past this rank's chunk count are stored empty). Nothing waits here;
 // layouts are checked before any store (fault bit 3: nothing stored).
-template <int S, typename T>
+template <int S, typename T, int W>
 __global__ void __launch_bounds__(kLdgThreads, 7)
 peer_span_kernel(const T* __restrict__ x, LdgSpan pl, int64_t slot_parts, Params p, PeerPtrs peers, int world,
                  int rank, unsigned char* own) {
@@ -490,19 +490,40 @@ peer_span_kernel(const T* __restrict__ x, LdgSpan pl, int64_t slot_parts, Params
     const unsigned int e = *reinterpret_cast<volatile unsigned int*>(&h->ep) + 1u;
     const int64_t par = e & 1u;
     const int lane = threadIdx.x & 31;
-    // lane r < world stores into rank r's buffer
-    float4* mine = lane < world ? reinterpret_cast<float4*>(peer_at(peers, lane) + kPeerHeaderBytes) : nullptr;
-    const int64_t gw = (int64_t)blockIdx.x * (kLdgThreads / 32) + (threadIdx.x >> 5);
-    const int64_t GW = (int64_t)gridDim.x * (kLdgThreads / 32);
-    const int64_t nitems = rows * slot_parts;
-    for (int64_t item = gw; item < nitems; item += GW) {
-        const int64_t row = item / slot_parts, part = item - row * slot_parts;
-        float4 v = make_float4(-NB200_INF, 0.f, 0.f, 0.f);  // an empty state (parts past this shard)
-        if (part < pl.nparts) {
-            const St w = span_item_state<S, T>(x, pl, row * pl.nparts + part, lane, p);
-            v = make_float4(w.m, w.acc, __int_as_float(w.seen), __int_as_float(w.status));
+    // slot of (row, part) in slot `rank` of any rank's buffer
+    auto slot = [&](unsigned char* buf, int64_t row, int64_t part) {
+        return reinterpret_cast<float4*>(buf + kPeerHeaderBytes) + ((par * rows + row) * world + rank) * slot_parts + part;
+    };
+    if constexpr (W == 1) {
+        // lane r < world stores into rank r's buffer
+        unsigned char* mine = lane < world ? peer_at(peers, lane) : nullptr;
+        const int64_t gw = (int64_t)blockIdx.x * (kLdgThreads / 32) + (threadIdx.x >> 5);
+        const int64_t GW = (int64_t)gridDim.x * (kLdgThreads / 32);
+        for (int64_t item = gw; item < pl.nitems; item += GW) {
+            const St w = span_item_state<S, T>(x, pl, item, lane, p);
+            const int64_t row = item / pl.nparts, part = item - row * pl.nparts;
+            if (mine)
+                peer_slot_store(slot(mine, row, part), make_float4(w.m, w.acc, __int_as_float(w.seen), __int_as_float(w.status)), e);
         }
-        if (mine) peer_slot_store(&mine[((par * rows + row) * world + rank) * slot_parts + part], v, e);
+    } else {
+        span_items_shared<S, T, W>(x, pl, p, [&](int64_t item, const St& w) {
+            const int64_t row = item / pl.nparts, part = item - row * pl.nparts;
+            const float4 v = make_float4(w.m, w.acc, __int_as_float(w.seen), __int_as_float(w.status));
+#pragma unroll
+            for (int r = 0; r < kMaxPeers; ++r)
+                if (r < world) peer_slot_store(slot(peers.p[r], row, part), v, e);
+        });
+    }
+    // parts past this shard's chunk count (unequal shard widths): empty states
+    const int64_t extra = slot_parts - pl.nparts;
+    if (extra > 0) {
+        const float4 v = make_float4(-NB200_INF, 0.f, 0.f, 0.f);
+        for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * extra * world;
+             i += (int64_t)gridDim.x * blockDim.x) {
+            const int r = (int)(i % world);
+            const int64_t j = i / world, row = j / extra, part = pl.nparts + (j - row * extra);
+            peer_slot_store(slot(peer_at(peers, r), row, part), v, e);
+        }
     }
 }
 
@@ -709,10 +730,12 @@ int peer_merge_dispatch(int sk, unsigned char* own, T* out, int64_t rows, int64_
 template <typename T>
 int peer_fold_dispatch(int sk, const T* x, const LdgSpan& pl, int64_t slot_parts, const PeerPtrs& pp, int world,
                        int rank, unsigned char* own, T* out, const Params& p, cudaStream_t st) {
+    // the items' decomposition of the partial fold (span_item_warps), so the states match it bit for bit
+    const int W = span_item_warps(pl.nitems, pl.cc / Elem<T>::V, sm_count());
     auto go = [&](auto k) {
         int occ = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kLdgThreads, 0) != cudaSuccess || occ < 1) occ = 1;
-        const int64_t warps = std::max<int64_t>(pl.rows * slot_parts, 1);
+        const int64_t warps = std::max<int64_t>(pl.nitems * W, 1);
         const int g = (int)std::max<int64_t>(1, std::min<int64_t>((warps + 3) / 4, (int64_t)sm_count() * occ));
         launch_pdl(k, (unsigned)g, kLdgThreads, 0, st, x, pl, slot_parts, p, pp, world, rank, own);
         count_launch();
@@ -720,7 +743,10 @@ int peer_fold_dispatch(int sk, const T* x, const LdgSpan& pl, int64_t slot_parts
         return rc ? rc : peer_merge_dispatch<T>(sk, own, out, pl.rows, slot_parts, world, p, st);
     };
     switch (sk) {
-#define X(S) case S: return go(peer_span_kernel<S, T>);
+#define X(S)                                                   \
+    case S:                                                    \
+        if (W == 4) return go(peer_span_kernel<S, T, 4>);      \
+        return go(peer_span_kernel<S, T, 1>);
         NB200_SPLIT_SKELETONS(X)
 #undef X
     }
@@ -898,6 +924,11 @@ int launch_peer_fold(int sk, const Params& p, const void* x, int dtype, int64_t 
         set_error("nb200_peer_fold: needs a contiguous, 16-byte aligned shard whose width and chunk are multiples of "
                   "%lld elements", (long long)V);
         return NB200_ERR_ARG;
+    }
+    if (chunk / V <= 32 * kSpanNV) {  // the partial fold holds such chunks as resident rows instead
+        set_error("nb200_peer_fold: chunks of at most %lld columns take the partial fold + nb200_peer_push form",
+                  (long long)(32 * kSpanNV * V));
+        return NB200_ERR_UNSUPPORTED;
     }
     const int64_t nlocal = (ncols_shard + chunk - 1) / chunk;
     if (nlocal > nparts) {

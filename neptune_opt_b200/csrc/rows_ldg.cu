@@ -142,6 +142,8 @@ __device__ __forceinline__ void span_store(const LdgSpan& pl, int64_t item, cons
 //                 forms one chunk's (resident_items_state: the producer reduced across the warp
 //                 first, every term against it, one warp sum; no per-lane repair and no 32-state
 //                 merge tree), the G items' warp reductions interleaved.
+//   G = -4        too few wide items to occupy the GPU (span_item_warps): the 4 warps of a CTA
+//                 share each item (span_items_shared).
 constexpr int kSpanStream = 0;
 
 template <int S, typename T, int G>
@@ -152,7 +154,9 @@ __global__ void __launch_bounds__(kLdgThreads) ldg_span_kernel(const T* __restri
     const int lane = threadIdx.x & 31;
     const int64_t gw = (int64_t)blockIdx.x * (kLdgThreads / 32) + (threadIdx.x >> 5);
     const int64_t GW = (int64_t)gridDim.x * (kLdgThreads / 32);
-    if constexpr (G == kSpanStream) {
+    if constexpr (G < 0) {
+        span_items_shared<S, T, -G>(x, pl, p, [&](int64_t item, const St& w) { span_store<S, T>(pl, item, w, p, states, out); });
+    } else if constexpr (G == kSpanStream) {
         for (int64_t item = gw; item < pl.nitems; item += GW) {
             const St w = span_item_state<S, T>(x, pl, item, lane, p);
             if (lane == 0) span_store<S, T>(pl, item, w, p, states, out);
@@ -177,14 +181,16 @@ int launch_ldg_span(int sk, const Params& p, const T* x, int64_t rows, int64_t c
                     int64_t cc, int64_t nparts, nb200_state* states, T* out, int finalize, cudaStream_t st) {
     LdgSpan pl{rows, srow, cb, ns, cc, nparts, rows * nparts, finalize};
     const int64_t nvec = cc / Elem<T>::V;  // vectors of the widest item
-    const int group = nvec <= 32 * kSpanNV / 4 ? 4 : nvec <= 32 * kSpanNV / 2 ? 2 : nvec <= 32 * kSpanNV ? 1
-                                                                                                      : kSpanStream;
+    int group = nvec <= 32 * kSpanNV / 4 ? 4 : nvec <= 32 * kSpanNV / 2 ? 2 : nvec <= 32 * kSpanNV ? 1
+                                                                                                : kSpanStream;
+    if (group == kSpanStream) group = -span_item_warps(pl.nitems, nvec, sm_count());  // -1: one warp per item
     int rc = NB200_OK;
     auto go = [&](auto k) {
         int occ = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, kLdgThreads, 0) != cudaSuccess || occ < 1) occ = 1;
-        const int64_t units = group > 1 ? (pl.nitems + group - 1) / group : pl.nitems;  // warp iterations
-        const int64_t need = (units + kLdgThreads / 32 - 1) / (kLdgThreads / 32);
+        // warps wanted: one per G items, one per item, or W per item
+        const int64_t warps = group > 1 ? (pl.nitems + group - 1) / group : pl.nitems * (group < 0 ? -group : 1);
+        const int64_t need = (warps + kLdgThreads / 32 - 1) / (kLdgThreads / 32);
         const int g = (int)std::min<int64_t>(need, (int64_t)sm_count() * occ);
         launch_pdl(k, (unsigned)std::max(g, 1), kLdgThreads, 0, st, x, pl, p, states, out);
         count_launch();
@@ -193,7 +199,8 @@ int launch_ldg_span(int sk, const Params& p, const T* x, int64_t rows, int64_t c
     switch (sk) {
 #define X(S)                                                                                   \
     case S:                                                                                    \
-        if (group == 4) go(ldg_span_kernel<S, T, 4>);                                          \
+        if (group == -4) go(ldg_span_kernel<S, T, -4>);                                        \
+        else if (group == 4) go(ldg_span_kernel<S, T, 4>);                                     \
         else if (group == 2) go(ldg_span_kernel<S, T, 2>);                                     \
         else if (group == 1) go(ldg_span_kernel<S, T, 1>);                                     \
         else go(ldg_span_kernel<S, T, kSpanStream>);                                           \
@@ -259,10 +266,6 @@ __device__ __forceinline__ void cluster_sync() {
 }
 
 // [v0, v1) of n vectors for part i of k (contiguous, ascending, sizes differing by at most one).
-__device__ __forceinline__ void split_range(int64_t n, int64_t k, int64_t i, int64_t& v0, int64_t& v1) {
-    v0 = n * i / k;
-    v1 = n * (i + 1) / k;
-}
 
 template <int S, typename T>
 __global__ void __launch_bounds__(kClThreads) cluster_fold_kernel(const T* __restrict__ x, int64_t rows,

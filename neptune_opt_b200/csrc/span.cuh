@@ -192,27 +192,92 @@ __device__ __forceinline__ void load_item(RegRow<NV>& blk, const T* __restrict__
     load_block<NV, T>(blk, reinterpret_cast<const uint4*>(x + row * pl.srow + lo), 0, (int)((hi - lo) / V), lane);
 }
 
-// Warp-merged state of span item `item` (row item / nparts, chunk item % nparts). Every lane of the
-// warp must call it; every lane returns the same state.
+// Warp-merged state of vectors [v0, v1) of a column span starting at `base`, folded in sub-blocks of
+// 32 x kSpanNV vectors. Every lane of the warp must call it; every lane returns the same state.
 template <int S, typename T>
-__device__ __forceinline__ St span_item_state(const T* __restrict__ x, const LdgSpan& pl, int64_t item, int lane,
-                                              const Params& p) {
-    constexpr int V = Elem<T>::V;
+__device__ __forceinline__ St span_range_state(const uint4* base, int v0, int v1, int lane, const Params& p) {
     constexpr bool kFast = S == NB200_LOGSUMEXP && sizeof(T) == 2;
-    const int64_t row = item / pl.nparts, part = item - row * pl.nparts;
-    const int64_t lo = pl.cb + part * pl.cc, hi = min(lo + pl.cc, pl.cb + pl.ns);
-    const uint4* base = reinterpret_cast<const uint4*>(x + row * pl.srow + lo);
-    const int nvec = (int)((hi - lo) / V);
     St run = empty_state();
-    for (int v0 = 0; v0 < nvec; v0 += 32 * kSpanNV) {
+    for (int v = v0; v < v1; v += 32 * kSpanNV) {
         RegRow<kSpanNV> blk;
-        load_block<kSpanNV, T>(blk, base, v0, nvec, lane);
+        load_block<kSpanNV, T>(blk, base, v, v1, lane);
         if constexpr (kFast)
             lse16_block<T>(blk, run, p);
         else
             run = merge_fast<S>(run, lane_state<S, T>(blk, p), p);
     }
     return warp_merge<S>(run, lane, p);
+}
+
+// First vector and vector count of span item `item` (row item / nparts, chunk item % nparts).
+template <typename T>
+__device__ __forceinline__ const uint4* span_item_base(const T* __restrict__ x, const LdgSpan& pl, int64_t item,
+                                                       int& nvec) {
+    constexpr int V = Elem<T>::V;
+    const int64_t row = item / pl.nparts, part = item - row * pl.nparts;
+    const int64_t lo = pl.cb + part * pl.cc, hi = min(lo + pl.cc, pl.cb + pl.ns);
+    nvec = (int)((hi - lo) / V);
+    return reinterpret_cast<const uint4*>(x + row * pl.srow + lo);
+}
+
+// Warp-merged state of span item `item`. Every lane of the warp must call it; every lane returns
+// the same state.
+template <int S, typename T>
+__device__ __forceinline__ St span_item_state(const T* __restrict__ x, const LdgSpan& pl, int64_t item, int lane,
+                                              const Params& p) {
+    int nvec;
+    const uint4* base = span_item_base<T>(x, pl, item, nvec);
+    return span_range_state<S, T>(base, 0, nvec, lane, p);
+}
+
+// Warps that fold one span item. One, unless the items are too few to occupy the GPU: then the 4
+// warps of a CTA share an item, each folding a contiguous quarter of its columns (at least one
+// sub-block each), and their 4 states merge in column order. The rule depends only on the item
+// count, the item width and the SM count, so every kernel that folds the same items (the split
+// plan's partial fold, the exchange's fused fold) decomposes them the same way and produces the
+// same states bit for bit. Resident warps are counted at 6 CTAs of kLdgThreads per SM. Measured on
+// B200 with bf16 16384-column chunks (split plan, interleaved A/B): 1024 items 15.7 -> 12.9 µs;
+// 2 warps per item at 2048 items neutral (20.0 vs 19.8 µs), so it is not used; at 4096 or more
+// items sharing costs more than the last uneven round of whole items (62.8 vs 51.3 µs at 8192).
+inline int span_item_warps(int64_t nitems, int64_t nvec, int sms) {
+    const int64_t slots = (int64_t)sms * 6 * (kLdgThreads / 32);
+    return (nvec >= 4 * 32 * kSpanNV && nitems * 4 <= slots + slots / 4) ? 4 : 1;
+}
+
+// Folds every span item with W warps per item (W = 2 or 4; the rule above uses 4) and hands each item's state to
+// sink(item, state), called by one thread per item. A CTA takes (kLdgThreads / 32) / W items at a
+// time; warp w folds part w % W of item w / W, lane 0 leaves its state in shared memory, and after
+// one barrier thread t merges item t's W states left to right. The shared states alternate
+// between two halves, so one barrier per round suffices. Every thread of the CTA must call it.
+template <int S, typename T, int W, class Sink>
+__device__ __forceinline__ void span_items_shared(const T* __restrict__ x, const LdgSpan& pl, const Params& p,
+                                                  Sink&& sink) {
+    constexpr int kPer = (kLdgThreads / 32) / W;
+    __shared__ float4 part_state[2][kLdgThreads / 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int half = 0;
+    for (int64_t unit = blockIdx.x; unit * kPer < pl.nitems; unit += gridDim.x, half ^= 1) {
+        const int64_t item = unit * kPer + warp / W;
+        if (item < pl.nitems) {
+            int nvec;
+            const uint4* base = span_item_base<T>(x, pl, item, nvec);
+            int64_t a, b;
+            split_range(nvec, W, warp % W, a, b);
+            const St w = span_range_state<S, T>(base, (int)a, (int)b, lane, p);
+            if (lane == 0)
+                part_state[half][warp] = make_float4(w.m, w.acc, __int_as_float(w.seen), __int_as_float(w.status));
+        }
+        __syncthreads();
+        if (threadIdx.x < kPer && unit * kPer + threadIdx.x < pl.nitems) {
+            St s = empty_state();
+#pragma unroll
+            for (int i = 0; i < W; ++i) {
+                const float4 v = part_state[half][threadIdx.x * W + i];
+                s = merge_fast<S>(s, St{v.x, v.y, __float_as_int(v.z), __float_as_int(v.w)}, p);
+            }
+            sink(unit * kPer + threadIdx.x, s);
+        }
+    }
 }
 
 }  // namespace nb200

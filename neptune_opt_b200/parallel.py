@@ -286,11 +286,12 @@ class PeerExchange:
     @staticmethod
     def fold_eligible(x_shard, chunk) -> bool:
         """Whether a shard can take the fused form (`fold`): contiguous 16-byte aligned rows whose
-        width, stride and chunk are multiples of 16 bytes."""
+        width, stride and chunk are multiples of 16 bytes, in chunks wider than 4 KB (narrower ones
+        the partial fold holds as resident rows, which the fused form does not)."""
         es = x_shard.element_size()
         return (x_shard.dim() == 2 and x_shard.stride(1) == 1 and x_shard.data_ptr() % 16 == 0
                 and (x_shard.shape[0] <= 1 or (x_shard.stride(0) * es) % 16 == 0)
-                and (x_shard.shape[1] * es) % 16 == 0 and (chunk * es) % 16 == 0)
+                and (x_shard.shape[1] * es) % 16 == 0 and (chunk * es) % 16 == 0 and chunk * es > 4096)
 
     def close(self):
         """Unmap the peers' buffers (collective: no rank may still be writing into another's)."""
