@@ -71,7 +71,10 @@ def _merge(lib, L, buf, rows, nparts, world, out):
                                 nparts, world, ctypes.c_void_p(out.data_ptr()), 0, _stream())
 
 
-def test_single_rank_exchange_equals_the_merge_kernel():
+@pytest.mark.parametrize("rows,nparts", [(ROWS, 3), (512, 4)])
+def test_single_rank_exchange_equals_the_merge_kernel(rows, nparts):
+    """192 chunk items: the 4 warps of a CTA share each item; 2048: one warp per item. The fused
+    form must decompose the items as the partial fold does in both cases."""
     import torch
 
     import neptune_opt_b200 as NB
@@ -81,25 +84,52 @@ def test_single_rank_exchange_equals_the_merge_kernel():
     torch.cuda.synchronize()
     L.stream_fault()
     gen = torch.Generator().manual_seed(41)
-    x = (torch.randn(ROWS, 3 * CHUNK, generator=gen) * 3).cuda()
-    nparts = 3
+    x = (torch.randn(rows, nparts * CHUNK, generator=gen) * 3).cuda()
     states = _states(lib, L, x, nparts)
-    _keep, buf = _buffer(lib, ROWS, 1, nparts)
-    _init(lib, L, buf, ROWS, 1, nparts)
-    want = torch.empty(ROWS, device="cuda")
+    _keep, buf = _buffer(lib, rows, 1, nparts)
+    _init(lib, L, buf, rows, 1, nparts)
+    want = torch.empty(rows, device="cuda")
     p = L.params_struct({"tiny": 0.0})
     L.check(lib.nb200_fold_merge(NB.SKELETONS["logsumexp"].id, ctypes.byref(p), ctypes.c_void_p(states.data_ptr()),
-                                 ROWS, nparts, nparts, 1, ctypes.c_void_p(want.data_ptr()), 0, _stream()), "merge")
+                                 rows, nparts, nparts, 1, ctypes.c_void_p(want.data_ptr()), 0, _stream()), "merge")
     for i in range(6):  # consecutive calls walk the epochs and parities, alternating the two forms
-        out = torch.full((ROWS,), float("nan"), device="cuda")
+        out = torch.full((rows,), float("nan"), device="cuda")
         if i % 2:
             L.check(_fold(lib, L, x, nparts, [buf], 0, buf, out), "peer fold")
         else:
-            L.check(_push(lib, states, ROWS, nparts, [buf], 0, buf), "push")
-            L.check(_merge(lib, L, buf, ROWS, nparts, 1, out), "peer merge")
+            L.check(_push(lib, states, rows, nparts, [buf], 0, buf), "push")
+            L.check(_merge(lib, L, buf, rows, nparts, 1, out), "peer merge")
         torch.cuda.synchronize()
         assert torch.equal(out, want), f"call {i}"
     assert L.stream_fault() == 0
+
+
+def test_fused_form_refuses_chunks_held_as_resident_rows():
+    """Chunks of 4 KB or less are folded by the partial fold as resident rows, a decomposition the
+    fused form does not have: it refuses them before launching anything."""
+    import torch
+
+    import neptune_opt_b200 as NB
+    import neptune_opt_b200._lib as L
+    from neptune_opt_b200.parallel import PeerExchange
+
+    lib = L.load()
+    torch.cuda.synchronize()
+    L.stream_fault()
+    x = torch.randn(ROWS, 4 * 1024, device="cuda")
+    _keep, buf = _buffer(lib, ROWS, 1, 4)
+    _init(lib, L, buf, ROWS, 1, 4)
+    out = torch.zeros(ROWS, device="cuda")
+    p = L.params_struct({"tiny": 0.0})
+    before = NB.launch_count()
+    rc = lib.nb200_peer_fold(NB.SKELETONS["logsumexp"].id, ctypes.byref(p), ctypes.c_void_p(x.data_ptr()), 0, ROWS,
+                             x.shape[1], x.shape[1], x.stride(0), 1024, 4,
+                             (ctypes.c_void_p * 1)(buf.data_ptr()), 1, 0, ctypes.c_void_p(buf.data_ptr()),
+                             ctypes.c_void_p(out.data_ptr()), _stream())
+    torch.cuda.synchronize()
+    assert rc == L.NB200_ERR_UNSUPPORTED and "push form" in L.last_error()
+    assert NB.launch_count() == before and int(out.count_nonzero()) == 0 and L.stream_fault() == 0
+    assert not PeerExchange.fold_eligible(x, 1024) and PeerExchange.fold_eligible(x, 2048)
 
 
 def _fold(lib, L, x, nparts, bufs, rank, own, out):
