@@ -619,6 +619,7 @@ def roofline(bytes_per_launch, ms, peaks, traffic):
     achieved = bytes_per_launch / (ms * 1e-3) / 1e9
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": round(achieved / peaks["hbm_gbs"], 4), "peak_source": peaks["source"] + " (burst copy)",
+            "frac_of_nominal": round(achieved / NOMINAL_HBM_GBS, 4),  # BASELINE's "% of 8 TB/s"
             "traffic": traffic}
 
 
