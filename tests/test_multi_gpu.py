@@ -40,7 +40,8 @@ def _rank_main(rank, world, port, result_path):
     from neptune_opt_b200 import _lib
     from neptune_opt_b200.parallel import PeerExchange, shard_rows, sharded_split_fold
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    # NVLS off: no NVLink multicast object is created for the collectives (the exchange uses none)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     td.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                           device_id=torch.device("cuda", rank))
