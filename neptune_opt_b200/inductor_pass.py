@@ -64,7 +64,7 @@ def fuse_casts(graph) -> int:
         if src is None or _dtype_of(src) not in lowp:
             continue
         users = list(node.users)
-        if len(users) != 1 or _cast_source(users[0], _dtype_of(src)) is not node:
+        if len(users) != 1 or _cast_source(users[0], _dtype_of(src)) is not node or "val" not in users[0].meta:
             continue
         narrow = users[0]
         widen = node.args[0]
