@@ -274,6 +274,8 @@ __global__ void __launch_bounds__(kClThreads) cluster_fold_kernel(const T* __res
     constexpr bool kFast = S == NB200_LOGSUMEXP && sizeof(T) == 2;
     __shared__ float4 cta_state[kClMax];
     __shared__ float4 warp_state[kClWarps];
+    pdl_wait();
+    pdl_trigger();
     const uint32_t crank = cluster_rank(), csize = cluster_size();
     const int64_t row = cluster_index();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -333,6 +335,8 @@ __global__ void __launch_bounds__(kClThreads) cluster_rms_kernel(const T* __rest
     constexpr int V = Elem<T>::V;
     __shared__ float part[kClMax];
     __shared__ float warp_sum_s[kClWarps];
+    pdl_wait();
+    pdl_trigger();
     const uint32_t crank = cluster_rank(), csize = cluster_size();
     const int64_t row = cluster_index();
     const bool live = row < rows;
@@ -427,8 +431,15 @@ static int cluster_ctas(K kernel, int64_t rows) {
         cudaGetLastError();
         max16.store(m, std::memory_order_relaxed);
     }
-    const int64_t want = std::max<int64_t>(2, (int64_t)sm_count() / std::max<int64_t>(rows, 1));
-    return (int)std::min<int64_t>(want, m ? 16 : 8);
+    // About 1.75 CTAs per SM in all, in power-of-two clusters: measured on B200 (logsumexp fp32,
+    // 16.8 MB, graph-timed) the best cluster size gave 256-296 CTAs for 16 to 128 rows -- [128,
+    // 32768] 7.9 µs at 2 CTAs per row against 9.7 at 4; [64, 65536] 8.0 at 4 against 9.1 at 2;
+    // [32, 131072] 8.2 at 8 against 9.4 at 4 -- and never fewer than 2 per row ([256, 16384] 9.1
+    // µs at 2, 13.0 at 4). Non-power-of-two clusters schedule worse ([64, 65536] at 7: 12.2 µs).
+    const int64_t want = std::min<int64_t>((7 * (int64_t)sm_count() / 4) / std::max<int64_t>(rows, 1), m ? 16 : 8);
+    int c = 2;
+    while (2 * c <= want) c *= 2;
+    return c;
 }
 
 template <typename K, typename... Args>
@@ -442,13 +453,17 @@ static int launch_cluster(K kernel, int64_t rows, int csize, cudaStream_t st, co
     cfg.gridDim = dim3((unsigned)(rows * csize));
     cfg.blockDim = dim3(kClThreads);
     cfg.stream = st;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = (unsigned)csize;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
+    // programmatic dependent launch, as the other kernels: the launch overlaps the previous
+    // kernel's tail, and the kernel's griddepcontrol.wait holds its reads until that kernel is done
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
     if (e != cudaSuccess) {
         cudaGetLastError();
