@@ -222,3 +222,20 @@ def test_segment_shard_edge_cases():
     assert sum(s.row_end - s.row_begin for s in shards) == 9
     one = parallel.shard_segments(torch.tensor([0]), 2, 1)
     assert one.seg_begin == one.seg_end == 0
+
+
+def test_fused_exchange_eligibility_follows_the_partial_folds_layout_rules():
+    """The fused form takes contiguous, 16-byte aligned shards in chunks wider than 4 KB; narrower
+    chunks (which the partial fold holds as resident rows), strided shards and unaligned widths go
+    to the partial fold + push form."""
+    import torch
+
+    from neptune_opt_b200.parallel import PeerExchange
+
+    f32 = torch.empty(64, 8192)
+    bf16 = torch.empty(64, 8192, dtype=torch.bfloat16)
+    assert PeerExchange.fold_eligible(f32, 2048) and not PeerExchange.fold_eligible(f32, 1024)
+    assert PeerExchange.fold_eligible(bf16, 4096) and not PeerExchange.fold_eligible(bf16, 2048)
+    assert not PeerExchange.fold_eligible(f32[:, ::2], 2048)        # strided columns
+    assert not PeerExchange.fold_eligible(f32[:, 1:4097], 2048)     # unaligned start
+    assert not PeerExchange.fold_eligible(torch.empty(64, 8190), 2048)  # width not a multiple of 16 B
